@@ -1,0 +1,424 @@
+"""Benchmark of the ElasticBit compressed-linear forward on B200.
+
+Workload (the decode GEMV sweep, one GPU): synthetic weights
+with the BASELINE scheme (per-row sigma log-uniform in [0.005, 0.05], 0.1 %
+entries x10) for (K, N) in {(4096, 4096), (4096, 14336), (14336, 4096)},
+compressed by the ElasticBit analyzer at thresholds {0.005, 0.01, 0.02} with 32
+calibration rows N(0, 1); activations FP16 N(0, 1), M in {1, 2, 4, 8, 16}.
+One step = all 45 (M, matrix) launches.  The 9 compressed matrices (~0.5 GB of
+codes) exceed the 126 MB L2 and are visited round-robin, so every launch
+streams its weights from HBM.
+
+Reported: ``value`` = algorithmic bytes / device time (GB/s), bytes per launch
+= ceil(N*K*b/8) + 4N + 2MK + 2MN (b = stored width); ``e2e`` = same bytes
+measured through the public API (RuntimeMatrix.linear) with pinned host
+inputs/outputs copied every launch; ``roofline`` for the decode kernel against
+the measured HBM copy bandwidth; ``cpu_baseline`` = the reference's
+``pytorch`` route restated on the host cores (F.linear over the dequantised
+weight, all threads) on a bounded sample.
+
+Multi-GPU (torchrun, --gpus N): every rank runs the same sweep on its own
+GPU (replicas; weak scaling); value = all ranks' bytes / max-over-ranks time.
+``--impl reference`` times the reference's CPU route only (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "qlinear GB/s (M≤16) & TFLOP/s (M=4096) vs roofline; decode tok/s @1/2/4/8 GPU"
+SHAPES = [(4096, 4096), (4096, 14336), (14336, 4096)]  # (K, N)
+THRESHOLDS = [0.005, 0.01, 0.02]
+MS = [1, 2, 4, 8, 16]
+
+
+def algorithmic_bytes(N: int, K: int, bits: int, M: int) -> int:
+    return math.ceil(N * K * bits / 8) + 4 * N + 2 * M * K + 2 * M * N
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+# clocks sampling (nvidia-smi) during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self) -> None:
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+def baseline_weights_gpu(N: int, K: int, seed: int, device):
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    log_sigma = torch.empty((N, 1), device=device).uniform_(math.log(0.005), math.log(0.05),
+                                                             generator=g)
+    w = torch.randn((N, K), device=device, generator=g) * torch.exp(log_sigma)
+    mask = torch.rand((N, K), device=device, generator=g) < 1.0e-3
+    w = torch.where(mask, w * 10.0, w)
+    return w.half()
+
+
+def build_matrices(device, seed0: int = 0):
+    """Compress the 9 (shape, threshold) matrices with the ElasticBit analyzer."""
+    import numpy as np
+    import torch
+
+    from mlbricks_b200.elasticbit.core import RuntimeMatrix, _selectBitsTorch
+
+    out = []
+    for si, (K, N) in enumerate(SHAPES):
+        w16 = baseline_weights_gpu(N, K, seed0 + si, device)
+        calib = np.random.default_rng(seed0 + 100 + si).standard_normal((32, K)).astype(np.float32)
+        for thr in THRESHOLDS:
+            bits, err, codes, scales = _selectBitsTorch(w16, calib, thr)
+            if bits <= 15:
+                m = RuntimeMatrix._compressSelectedCodes(codes, scales, bits, thr, err,
+                                                         decodePolicy="hardwareNative")
+            else:
+                m = RuntimeMatrix._compressSelected(w16.float(), bits, thr, err)
+            out.append({"K": K, "N": N, "threshold": thr, "bits": bits, "matrix": m})
+            del codes, scales
+        del w16
+        torch.cuda.empty_cache()
+    return out
+
+
+def run_gpu(args) -> None:
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+
+    from mlbricks_b200 import _ebx
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=device)
+    lib = _ebx.load()
+
+    mats = build_matrices(device)
+    torch.cuda.synchronize()
+
+    # inputs / outputs (device) for every (M, matrix)
+    xs = {M: {K: torch.randn((M, K), device=device, dtype=torch.float16) for K in {4096, 14336}}
+          for M in MS}
+    ys = {M: {N: torch.empty((M, N), device=device, dtype=torch.float16) for N in {4096, 14336}}
+          for M in MS}
+    launches = [(M, e) for M in MS for e in mats]
+    step_bytes = sum(algorithmic_bytes(e["N"], e["K"], e["bits"], M) for M, e in launches)
+    handles = {id(e): ctypes.c_void_p(e["matrix"]._native.handle) for e in mats}
+
+    stream = torch.cuda.Stream(device)
+    sptr = int(stream.cuda_stream)
+
+    def launch(M, e):
+        _ebx.check(lib.ebx_linear(handles[id(e)], xs[M][e["K"]].data_ptr(), M, None,
+                                  ys[M][e["N"]].data_ptr(), None, None, 0, sptr))
+
+    # warm-up (also configures kernel attributes before capture)
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 1)):
+            for M, e in launches:
+                launch(M, e)
+    stream.synchronize()
+
+    # one step captured as a CUDA graph with an event pair around every launch
+    nL = len(launches)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(nL)]
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i, (M, e) in enumerate(launches):
+            ev[i][0].record(stream)
+            launch(M, e)
+            ev[i][1].record(stream)
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    stream.synchronize()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    per_launch = [0.0] * nL
+    t0.record(stream)
+    for _ in range(args.steps):
+        graph.replay()
+    t1.record(stream)
+    stream.synchronize()
+    total_ms = t0.elapsed_time(t1)
+    # the graph's internal events hold the last replay's per-launch times
+    for i in range(nL):
+        per_launch[i] = ev[i][0].elapsed_time(ev[i][1])
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+
+    t = torch.tensor([total_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    ms_per_step = max_ms / args.steps
+    value = step_bytes * world * args.steps / (max_ms * 1e-3) / 1e9
+
+    # roofline of the decode kernel: algorithmic bytes / summed launch durations
+    kern_ms = sum(per_launch)
+    achieved = step_bytes / (kern_ms * 1e-3) / 1e9
+    pk = peaks()
+    by_m = {}
+    for i, (M, e) in enumerate(launches):
+        b = algorithmic_bytes(e["N"], e["K"], e["bits"], M)
+        by_m.setdefault(M, [0, 0.0])
+        by_m[M][0] += b
+        by_m[M][1] += per_launch[i]
+    per_m = {str(M): round(v[0] / (v[1] * 1e-3) / 1e9, 1) for M, v in by_m.items()}
+
+    # e2e through the public API with pinned host buffers
+    e2e = run_e2e(mats, device, args)
+
+    result = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp16 activations x b-bit codes (b=" +
+                 ",".join(str(b) for b in sorted({e["bits"] for e in mats})) + "), fp32 accumulate",
+        "data": "synthetic (BASELINE weight scheme, seeded; no dataset)",
+        "config": {
+            "workload": "config2 decode GEMV sweep: M in {1,2,4,8,16} x (K,N) in "
+                        "{(4096,4096),(4096,14336),(14336,4096)} x threshold {0.005,0.01,0.02}",
+            "matrices": [{"K": e["K"], "N": e["N"], "threshold": e["threshold"], "bits": e["bits"]}
+                         for e in mats],
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+            "l2": "inputs larger than L2: 9 matrices (~0.5 GB codes) visited round-robin",
+            "timing": "CUDA graph of one step replayed; CUDA events on the launching stream",
+            "per_M_GBps": per_m,
+        },
+        "roofline": {
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+            "peak_source": pk["source"], "kernel": "ebx decode_kernel (M<=16)",
+        },
+        "e2e": e2e,
+        "gpu_launches": nL * args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result))
+
+
+def run_e2e(mats, device, args) -> dict:
+    """Same bytes metric through RuntimeMatrix.linear with host I/O each launch."""
+    import torch
+
+    xs_h = {M: {K: torch.randn((M, K), dtype=torch.float16).pin_memory() for K in {4096, 14336}}
+            for M in MS}
+    ys_h = {M: {N: torch.empty((M, N), dtype=torch.float16).pin_memory() for N in {4096, 14336}}
+            for M in MS}
+    launches = [(M, e) for M in MS for e in mats]
+    step_bytes = sum(algorithmic_bytes(e["N"], e["K"], e["bits"], M) for M, e in launches)
+    h2d = sum(2 * M * e["K"] for M, e in launches)
+    d2h = sum(2 * M * e["N"] for M, e in launches)
+
+    def step():
+        for M, e in launches:
+            x = xs_h[M][e["K"]].to(device, non_blocking=True)
+            y = e["matrix"].linear(x)
+            ys_h[M][e["N"]].copy_(y, non_blocking=True)
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    torch.cuda.synchronize()
+    steps = max(1, min(args.steps, 20))
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        step()
+    b.record()
+    b.synchronize()
+    ms = a.elapsed_time(b)
+    return {"value": round(step_bytes * steps / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "ms_per_step": round(ms / steps, 4), "api": "RuntimeMatrix.linear"}
+
+
+# ---------------------------------------------------------------------------
+# CPU: the reference's `pytorch` route restated on the host cores
+# ---------------------------------------------------------------------------
+def cpu_baseline(seconds: float = 8.0, shape=(4096, 4096), bits: int = 10) -> dict:
+    """F.linear(x32, W32) on the host with all threads over the exactly
+    dequantised weight (prepared once, untimed), M in {1, 16}; GB/s of the same
+    algorithmic bytes.  Sample: 4096x4096 at 10 bits, repeated for ~`seconds`."""
+    import numpy as np
+    import torch
+
+    from oracle import oracle as O
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    K, N = shape
+    w = O.baseline_weights(N, K, seed=0)
+    s = O.row_scales(w, bits)
+    q = O.quantize(w, s, bits)
+    W = torch.from_numpy(O.dequantize_codes(q, s).astype(np.float32))
+    total_bytes = 0
+    t_total = 0.0
+    results = {}
+    for M in (1, 16):
+        x = torch.from_numpy(O.normal((M, K), seed=M).astype(np.float16).astype(np.float32))
+        torch.nn.functional.linear(x, W)
+        n = 0
+        t0 = time.perf_counter()
+        while True:
+            torch.nn.functional.linear(x, W)
+            n += 1
+            el = time.perf_counter() - t0
+            if el > seconds / 2:
+                break
+        b = algorithmic_bytes(N, K, bits, M) * n
+        results[str(M)] = round(b / el / 1e9, 3)
+        total_bytes += b
+        t_total += el
+    return {"value": round(total_bytes / t_total / 1e9, 3), "unit": "GB/s", "cores": threads,
+            "kind": "port",
+            "sample": f"F.linear fp32 on host, {N}x{K} dequantised {bits}-bit weight, M in {{1,16}}, "
+                      f"{t_total:.1f}s; per-M GB/s {results}"}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    secs = max(2.0, min(20.0, 2.0 * (args.steps + args.warmup)))
+    cb = cpu_baseline(seconds=secs)
+    print(json.dumps({
+        "impl": "reference",
+        "metric": METRIC, "value": cb["value"], "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (host)",
+        "data": "synthetic (BASELINE weight scheme, seeded)",
+        "config": {"workload": "config2 decode GEMV sweep sample (4096x4096, M in {1,16})",
+                   "route": "reference pytorch route restated on host cores (no CPU path exists "
+                            "in the reference; its forward is CUDA-only)"},
+        "cpu_baseline": cb,
+        "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }))
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ebx", choices=["ebx", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,171 @@
+/*
+ * ebx.h -- C ABI of libebx, the B200-native ElasticBit compressed-linear runtime.
+ *
+ * Plain C: opaque handles, raw pointers, sizes and integer status codes; no
+ * C++ exceptions or torch types cross this boundary.  `stream` arguments are
+ * cudaStream_t values passed as void* (NULL = legacy default stream).  Every
+ * device-side entry point is stream-ordered.  Calls on one matrix handle from
+ * several host threads are safe as long as each call uses its own output
+ * buffers; creation/destruction of a handle must not race with its use.
+ *
+ * Reference interfaces replaced (paths inside the MLBricks tree):
+ *   mlbricks/elasticbit/csrc/elasticbit_runtime.cu  -- pybind module _C,
+ *       class RuntimeMatrix (cu:714-1384, bindings cu:1411-1469)
+ *   mlbricks/bolt/ops.cpp:1012-1043,1132  -- op mlbricks_native::
+ *       elastic_linear_packed, kernel mlbricks/bolt/ops_cuda.cu:2708-2796
+ */
+#ifndef EBX_H_
+#define EBX_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define EBX_API __attribute__((visibility("default")))
+#else
+#define EBX_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  ebx_last_error() gives the message of the calling thread's
+ * most recent failure. */
+typedef enum {
+    EBX_OK = 0,
+    EBX_ERR_INVALID = 1,     /* bad argument (reference: std::invalid_argument -> ValueError) */
+    EBX_ERR_CUDA = 2,        /* CUDA runtime failure (reference: CUDA_CHECK -> RuntimeError)  */
+    EBX_ERR_UNSUPPORTED = 3, /* shape/width this build does not execute                        */
+    EBX_ERR_WORKSPACE = 4,   /* caller workspace missing or too small                          */
+    EBX_ERR_CODE_RANGE = 5   /* a prequantized code lies outside [-qmax, qmax]                 */
+} ebx_status;
+
+typedef struct ebx_matrix ebx_matrix;
+
+/* Matrix description returned by ebx_matrix_query. */
+typedef struct {
+    int32_t rows;              /* N (out_features)                                  */
+    int32_t cols;              /* K (in_features)                                   */
+    int32_t storage_bits;      /* 3..15, or 16 for the FP16 fallback                */
+    int32_t execution_width;   /* 16, 8 or 4 (see ebx_matrix_set_execution_width)   */
+    int32_t device;            /* CUDA ordinal that owns the buffers                */
+    int32_t reserved;
+    uint64_t payload_bytes;    /* MLB4 payload size: ceil(N*K*b/8), or 2*N*K for b=16 */
+    uint64_t device_bytes;     /* resident device bytes (tile codes + scales)       */
+} ebx_matrix_info;
+
+/* Library version string, e.g. "ebx 0.1.0 sm_100a". */
+EBX_API const char* ebx_version(void);
+
+/* Copies the calling thread's last error message into buf (NUL-terminated,
+ * truncated to len-1) and returns the full message length. */
+EBX_API size_t ebx_last_error(char* buf, size_t len);
+
+/* Create from the analyzer's selected signed codes q (int16, row-major
+ * [rows, cols], DEVICE pointer) and per-row fp32 scales (DEVICE pointer),
+ * 3 <= bits <= 15.  Packing runs on the device.
+ * Replaces RuntimeMatrix._compressSelectedCodes -> pack_exact_codes
+ * (elasticbit_runtime.cu:778-808, 150-186).  Returns EBX_ERR_CODE_RANGE when
+ * any |q| > qmax (cu:168-170).  Synchronizes `stream`. */
+EBX_API ebx_status ebx_matrix_create_from_codes(const int16_t* codes, const float* scales, int32_t rows,
+                                        int32_t cols, int32_t bits, int32_t device, void* stream,
+                                        ebx_matrix** out);
+
+/* Create from an MLB4 payload (LSB-first bitstream of q+qmax codes, or raw
+ * fp16 for bits == 16) and per-row scales (ignored for bits == 16).
+ * `on_device` = 1: both pointers are device memory; 0: host memory.
+ * Replaces the RuntimeMatrix(rows, cols, bits, ..., scales, payload)
+ * constructor behind RuntimeMatrix.load (cu:810-871, 1143-1157). */
+EBX_API ebx_status ebx_matrix_create_from_payload(const void* payload, uint64_t payload_bytes,
+                                          const float* scales, int32_t rows, int32_t cols,
+                                          int32_t bits, int32_t on_device, int32_t device,
+                                          void* stream, ebx_matrix** out);
+
+/* Create a 16-bit (FP16 fallback) matrix from row-major fp16 weights (DEVICE).
+ * Replaces RuntimeMatrix._compressSelected with selectedBits = 16
+ * (cu:748-776, pack_exact_weights cu:113-120). */
+EBX_API ebx_status ebx_matrix_create_from_fp16(const void* weights, int32_t rows, int32_t cols,
+                                       int32_t device, void* stream, ebx_matrix** out);
+
+/* Release the handle and its device buffers (cu:716, 1370-1383). */
+EBX_API ebx_status ebx_matrix_destroy(ebx_matrix* m);
+
+EBX_API ebx_status ebx_matrix_query(const ebx_matrix* m, ebx_matrix_info* info);
+
+/* Select execution semantics (cu:240-244, 1174-1178, 1315-1334):
+ * 16 = fp16(q*s) operands (W16A16 / fullPrecision), 8 or 4 = integer codes with
+ * the row scale applied after accumulation (W8A16 / W4A16).  8 requires
+ * bits <= 8, 4 requires bits <= 4.  The stored code is the same either way. */
+EBX_API ebx_status ebx_matrix_set_execution_width(ebx_matrix* m, int32_t width);
+
+/* Write the MLB4 payload bitstream (payload_bytes bytes) to `dst` (DEVICE).
+ * Replaces the payload half of RuntimeMatrix.save (cu:1024-1049). */
+EBX_API ebx_status ebx_matrix_export_payload(const ebx_matrix* m, void* dst, uint64_t dst_bytes,
+                                     void* stream);
+
+/* Copy the rows fp32 scales to `dst` (DEVICE).  No-op for bits == 16. */
+EBX_API ebx_status ebx_matrix_export_scales(const ebx_matrix* m, float* dst, void* stream);
+
+/* Exact dequantised weight, row-major fp16 [rows, cols] into `dst` (DEVICE):
+ * W[n,k] = fp16_rn(fp32(q) * s_n).  Replaces RuntimeMatrix._materializeTorch
+ * (cu:982-1022) and the values of RuntimeMatrix.dequantize (cu:208-238). */
+EBX_API ebx_status ebx_matrix_materialize(const ebx_matrix* m, void* dst, void* stream);
+
+/* Workspace bytes ebx_linear needs for M activation rows (0 when none). */
+EBX_API uint64_t ebx_linear_workspace_bytes(const ebx_matrix* m, int64_t M);
+
+/* y[M, rows] = x[M, cols] * W^T (+ bias), all fp16 DEVICE pointers, row-major,
+ * contiguous; bias may be NULL; y32 (fp32 [M, rows]) may be NULL and receives
+ * the fp32 value that was rounded into y.  Replaces _ElasticLinear.forward's
+ * two routes (core.py:446-471): RuntimeMatrix.forwardTorch (cu:902-931) for
+ * M = 1 and materialise + F.linear for M > 1. */
+EBX_API ebx_status ebx_linear(const ebx_matrix* m, const void* x, int64_t M, const void* bias, void* y,
+                      float* y32, void* workspace, uint64_t workspace_bytes, void* stream);
+
+/* Workspace bytes for ebx_analyze (fp16 reference outputs + per-row partial
+ * sums). */
+EBX_API uint64_t ebx_analyze_workspace_bytes(int32_t rows, int32_t samples);
+
+/* Matrix-path width analysis on the device: for every width 3..16 the
+ * hardwareNative and fullPrecision relative-L2 errors against the fp16
+ * reference, written to hw_err[14] / full_err[14] (DEVICE, index bits-3).
+ * weights fp32 [rows, cols], calib fp32 [samples, cols] (DEVICE).
+ * Replaces the host analyzer analyze_all_bits (elasticbit_runtime.cu:280-415)
+ * behind _C.analyze and RuntimeMatrix.compress (cu:438-483, 720-746). */
+EBX_API ebx_status ebx_analyze(const float* weights, int32_t rows, int32_t cols, const float* calib,
+                       int32_t samples, double* hw_err, double* full_err, void* workspace,
+                       uint64_t workspace_bytes, void* stream);
+
+/* Quantise fp32 weights [rows, cols] (DEVICE) for width 3..15: per-row scale
+ * max|w|/qmax (1 for a zero row) and codes clamp(rint(w/s), +-qmax), written
+ * to codes (int16 DEVICE) and scales (fp32 DEVICE).  Replaces make_row_scales +
+ * quantize_scalar (cu:77-101) inside RuntimeMatrix._compressSelected. */
+EBX_API ebx_status ebx_quantize(const float* weights, int32_t rows, int32_t cols, int32_t bits,
+                        int16_t* codes, float* scales, void* stream);
+
+/* fp32 -> fp16 (round to nearest even) of n values, DEVICE to DEVICE
+ * (the 16-bit storage of pack_exact_weights, cu:113-120). */
+EBX_API ebx_status ebx_weights_to_fp16(const float* weights, int64_t n, void* out, void* stream);
+
+/* FNV-1a 64 of a HOST byte range: the MLB4 scale/payload checksum
+ * (elasticbit_runtime.cu:682-690, written at cu:1036-1037, checked at
+ * cu:857-863). */
+EBX_API uint64_t ebx_fnv1a64(const void* data, uint64_t size);
+
+/* Drop-in for the dispatcher op mlbricks_native::elastic_linear_packed
+ * (ops.cpp:1012-1043; ops_cuda.cu:2708-2796): packed LSB-first codes with
+ * q = uq - 2^(bits-1), 2 <= bits <= 8, scale index = flat_index / group_size.
+ * dtype codes: 0 = fp32, 1 = fp16, 2 = bf16.  x, bias and out share x_dtype;
+ * bias may be NULL.  rows = x.numel / in_features. */
+EBX_API ebx_status ebx_elastic_linear_packed(const void* x, int32_t x_dtype, int64_t rows,
+                                     const uint8_t* packed, const void* scales,
+                                     int32_t scale_dtype, const void* bias, int32_t bits,
+                                     int64_t group_size, int64_t out_features,
+                                     int64_t in_features, void* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EBX_H_ */

@@ -1,0 +1,430 @@
+// ebx_capi.cu -- the extern "C" boundary of libebx (declared in include/ebx.h).
+//
+// Ownership mirrors the reference RuntimeMatrix (elasticbit_runtime.cu:714-
+// 1384): the handle owns its device buffers and frees them on destroy.  Unlike
+// the reference, no host copy of the payload is kept and nothing is unpacked on
+// the host: the device holds only the exact-width tile codes and fp32 scales.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+
+#include "../../include/ebx.h"
+#include "ebx_common.cuh"
+#include "ebx_internal.h"
+
+struct ebx_matrix {
+    ebx::Matrix m;
+};
+
+namespace ebx {
+
+static thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+}  // namespace ebx
+
+namespace {
+
+using ebx::set_error;
+
+ebx_status cuda_fail(cudaError_t e, const char* what) {
+    set_error(std::string("CUDA error: ") + cudaGetErrorString(e) + " in " + what);
+    return EBX_ERR_CUDA;
+}
+
+#define EBX_CUDA(call)                                 \
+    do {                                               \
+        cudaError_t e__ = (call);                      \
+        if (e__ != cudaSuccess) return cuda_fail(e__, #call); \
+    } while (0)
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = false;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) == cudaSuccess && (prev == dev || cudaSetDevice(dev) == cudaSuccess))
+            ok = true;
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+uint64_t payload_bytes_for(int rows, int cols, int bits) {
+    const uint64_t count = uint64_t(rows) * uint64_t(cols);
+    return bits == 16 ? count * 2 : (count * uint64_t(bits) + 7) / 8;
+}
+
+ebx_status validate_shape(int rows, int cols, int bits, bool allow16) {
+    if (rows <= 0 || cols <= 0) {
+        set_error("invalid ElasticBit matrix dimensions");
+        return EBX_ERR_INVALID;
+    }
+    if (bits < ebx::kMinBits || bits > (allow16 ? 16 : ebx::kMaxBits)) {
+        set_error(allow16 ? "ElasticBit storage bits must be between 3 and 16"
+                          : "prequantized codes require 3..15-bit storage");
+        return EBX_ERR_INVALID;
+    }
+    return EBX_OK;
+}
+
+// Allocates the handle and its tile/scale buffers (zeroed).
+ebx_status alloc_matrix(int rows, int cols, int bits, int device, ebx_matrix** out) {
+    ebx_matrix* h = new (std::nothrow) ebx_matrix();
+    if (!h) {
+        set_error("out of host memory");
+        return EBX_ERR_INVALID;
+    }
+    ebx::Matrix& m = h->m;
+    m.rows = rows;
+    m.cols = cols;
+    m.bits = bits;
+    m.device = device;
+    m.exec_width = 16;
+    m.kt = ebx::round_up(cols, ebx::kKTile) / ebx::kKTile;
+    m.groups = ebx::round_up(rows, ebx::kRowGroup) / ebx::kRowGroup;
+    m.tiles_bytes = size_t(m.groups * m.kt * ebx::tile_bytes(bits));
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&m.tiles), m.tiles_bytes);
+    if (e == cudaSuccess && bits != 16)
+        e = cudaMalloc(reinterpret_cast<void**>(&m.scales), sizeof(float) * size_t(rows));
+    if (e != cudaSuccess) {
+        if (m.tiles) cudaFree(m.tiles);
+        delete h;
+        return cuda_fail(e, "cudaMalloc(matrix buffers)");
+    }
+    *out = h;
+    return EBX_OK;
+}
+
+void free_matrix(ebx_matrix* h) {
+    if (!h) return;
+    DeviceGuard g(h->m.device);
+    if (h->m.tiles) cudaFree(h->m.tiles);
+    if (h->m.scales) cudaFree(h->m.scales);
+    delete h;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ebx_version(void) { return "ebx 0.1.0 sm_100a"; }
+
+size_t ebx_last_error(char* buf, size_t len) {
+    const std::string& s = ebx::g_last_error;
+    if (buf && len) {
+        const size_t n = s.size() < len - 1 ? s.size() : len - 1;
+        std::memcpy(buf, s.data(), n);
+        buf[n] = '\0';
+    }
+    return s.size();
+}
+
+ebx_status ebx_matrix_create_from_codes(const int16_t* codes, const float* scales, int32_t rows,
+                                        int32_t cols, int32_t bits, int32_t device, void* stream,
+                                        ebx_matrix** out) {
+    if (!out || !codes || !scales) {
+        set_error("codes, scales and out must be non-null");
+        return EBX_ERR_INVALID;
+    }
+    *out = nullptr;
+    ebx_status st = validate_shape(rows, cols, bits, false);
+    if (st != EBX_OK) return st;
+    DeviceGuard g(device);
+    if (!g.ok) return cuda_fail(cudaErrorInvalidDevice, "cudaSetDevice");
+    ebx_matrix* h = nullptr;
+    st = alloc_matrix(rows, cols, bits, device, &h);
+    if (st != EBX_OK) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int* bad = nullptr;
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&bad), sizeof(int));
+    if (e == cudaSuccess) e = cudaMemsetAsync(bad, 0, sizeof(int), s);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(h->m.scales, scales, sizeof(float) * size_t(rows),
+                            cudaMemcpyDeviceToDevice, s);
+    if (e == cudaSuccess) e = ebx::launch_codes_to_tiles(h->m, codes, bad, s);
+    int bad_host = 0;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&bad_host, bad, sizeof(int), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (bad) cudaFree(bad);
+    if (e != cudaSuccess) {
+        free_matrix(h);
+        return cuda_fail(e, "ebx_matrix_create_from_codes");
+    }
+    if (bad_host) {
+        free_matrix(h);
+        set_error("prequantized ElasticBit code exceeds selected bit range");
+        return EBX_ERR_CODE_RANGE;
+    }
+    *out = h;
+    return EBX_OK;
+}
+
+ebx_status ebx_matrix_create_from_payload(const void* payload, uint64_t payload_bytes,
+                                          const float* scales, int32_t rows, int32_t cols,
+                                          int32_t bits, int32_t on_device, int32_t device,
+                                          void* stream, ebx_matrix** out) {
+    if (!out || !payload || (bits != 16 && !scales)) {
+        set_error("payload, scales and out must be non-null");
+        return EBX_ERR_INVALID;
+    }
+    *out = nullptr;
+    ebx_status st = validate_shape(rows, cols, bits, true);
+    if (st != EBX_OK) return st;
+    if (payload_bytes != payload_bytes_for(rows, cols, bits)) {
+        set_error("invalid ElasticBit MLB4 metadata");
+        return EBX_ERR_INVALID;
+    }
+    DeviceGuard g(device);
+    if (!g.ok) return cuda_fail(cudaErrorInvalidDevice, "cudaSetDevice");
+    ebx_matrix* h = nullptr;
+    st = alloc_matrix(rows, cols, bits, device, &h);
+    if (st != EBX_OK) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const uint8_t* dpay = static_cast<const uint8_t*>(payload);
+    uint8_t* staged = nullptr;
+    cudaError_t e = cudaSuccess;
+    if (!on_device) {
+        e = cudaMalloc(reinterpret_cast<void**>(&staged), payload_bytes);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(staged, payload, payload_bytes, cudaMemcpyHostToDevice, s);
+        dpay = staged;
+    }
+    if (e == cudaSuccess && bits != 16)
+        e = cudaMemcpyAsync(h->m.scales, scales, sizeof(float) * size_t(rows),
+                            on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) {
+        e = bits == 16 ? ebx::launch_fp16_to_tiles(h->m, reinterpret_cast<const uint16_t*>(dpay), s)
+                       : ebx::launch_payload_to_tiles(h->m, dpay, payload_bytes, s);
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (staged) cudaFree(staged);
+    if (e != cudaSuccess) {
+        free_matrix(h);
+        return cuda_fail(e, "ebx_matrix_create_from_payload");
+    }
+    *out = h;
+    return EBX_OK;
+}
+
+ebx_status ebx_matrix_create_from_fp16(const void* weights, int32_t rows, int32_t cols,
+                                       int32_t device, void* stream, ebx_matrix** out) {
+    return ebx_matrix_create_from_payload(weights, payload_bytes_for(rows, cols, 16), nullptr,
+                                          rows, cols, 16, 1, device, stream, out);
+}
+
+ebx_status ebx_matrix_destroy(ebx_matrix* m) {
+    free_matrix(m);
+    return EBX_OK;
+}
+
+ebx_status ebx_matrix_query(const ebx_matrix* h, ebx_matrix_info* info) {
+    if (!h || !info) {
+        set_error("null argument");
+        return EBX_ERR_INVALID;
+    }
+    const ebx::Matrix& m = h->m;
+    info->rows = m.rows;
+    info->cols = m.cols;
+    info->storage_bits = m.bits;
+    info->execution_width = m.exec_width;
+    info->device = m.device;
+    info->reserved = 0;
+    info->payload_bytes = payload_bytes_for(m.rows, m.cols, m.bits);
+    info->device_bytes = m.tiles_bytes + (m.scales ? sizeof(float) * size_t(m.rows) : 0);
+    return EBX_OK;
+}
+
+ebx_status ebx_matrix_set_execution_width(ebx_matrix* h, int32_t width) {
+    if (!h) {
+        set_error("null matrix");
+        return EBX_ERR_INVALID;
+    }
+    if (width != 4 && width != 8 && width != 16) {
+        set_error("ElasticBit execution width must be 4, 8, or 16");
+        return EBX_ERR_INVALID;
+    }
+    if (width == 4 && h->m.bits > 4) {
+        set_error("W4A16 cannot represent this ElasticBit storage width");
+        return EBX_ERR_INVALID;
+    }
+    if (width == 8 && h->m.bits > 8) {
+        set_error("W8A16 cannot represent this ElasticBit storage width");
+        return EBX_ERR_INVALID;
+    }
+    h->m.exec_width = width;
+    return EBX_OK;
+}
+
+ebx_status ebx_matrix_export_payload(const ebx_matrix* h, void* dst, uint64_t dst_bytes,
+                                     void* stream) {
+    if (!h || !dst) {
+        set_error("null argument");
+        return EBX_ERR_INVALID;
+    }
+    const ebx::Matrix& m = h->m;
+    const uint64_t need = payload_bytes_for(m.rows, m.cols, m.bits);
+    if (dst_bytes < need) {
+        set_error("payload destination too small");
+        return EBX_ERR_INVALID;
+    }
+    DeviceGuard g(m.device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (m.bits == 16) {
+        EBX_CUDA(ebx::launch_materialize(m, static_cast<uint16_t*>(dst), s));
+    } else {
+        EBX_CUDA(ebx::launch_tiles_to_payload(m, static_cast<uint8_t*>(dst), need, s));
+    }
+    return EBX_OK;
+}
+
+ebx_status ebx_matrix_export_scales(const ebx_matrix* h, float* dst, void* stream) {
+    if (!h || !dst) {
+        set_error("null argument");
+        return EBX_ERR_INVALID;
+    }
+    if (!h->m.scales) return EBX_OK;
+    DeviceGuard g(h->m.device);
+    EBX_CUDA(cudaMemcpyAsync(dst, h->m.scales, sizeof(float) * size_t(h->m.rows),
+                             cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream)));
+    return EBX_OK;
+}
+
+ebx_status ebx_matrix_materialize(const ebx_matrix* h, void* dst, void* stream) {
+    if (!h || !dst) {
+        set_error("null argument");
+        return EBX_ERR_INVALID;
+    }
+    DeviceGuard g(h->m.device);
+    EBX_CUDA(ebx::launch_materialize(h->m, static_cast<uint16_t*>(dst),
+                                     static_cast<cudaStream_t>(stream)));
+    return EBX_OK;
+}
+
+uint64_t ebx_linear_workspace_bytes(const ebx_matrix* h, int64_t M) {
+    (void)h;
+    (void)M;
+    return 0;
+}
+
+ebx_status ebx_linear(const ebx_matrix* h, const void* x, int64_t M, const void* bias, void* y,
+                      float* y32, void* workspace, uint64_t workspace_bytes, void* stream) {
+    (void)workspace;
+    (void)workspace_bytes;
+    if (!h || (M > 0 && (!x || !y))) {
+        set_error("null argument");
+        return EBX_ERR_INVALID;
+    }
+    if (M < 0) {
+        set_error("M must be non-negative");
+        return EBX_ERR_INVALID;
+    }
+    if (M == 0) return EBX_OK;
+    DeviceGuard g(h->m.device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    EBX_CUDA(ebx::launch_decode(h->m, static_cast<const uint16_t*>(x), M,
+                                static_cast<const uint16_t*>(bias), static_cast<uint16_t*>(y), y32,
+                                s));
+    return EBX_OK;
+}
+
+uint64_t ebx_fnv1a64(const void* data, uint64_t size) {
+    const uint8_t* p = static_cast<const uint8_t*>(data);
+    uint64_t h = 1469598103934665603ull;
+    for (uint64_t i = 0; i < size; ++i) {
+        h ^= uint64_t(p[i]);
+        h *= 1099511628211ull;
+    }
+    return h;
+}
+
+uint64_t ebx_analyze_workspace_bytes(int32_t rows, int32_t samples) {
+    if (rows <= 0 || samples <= 0) return 0;
+    const uint64_t ref = ebx::round_up(uint64_t(rows) * uint64_t(samples) * 4, 256);
+    return ref + uint64_t(rows) * 14 * 3 * 8;
+}
+
+ebx_status ebx_analyze(const float* weights, int32_t rows, int32_t cols, const float* calib,
+                       int32_t samples, double* hw_err, double* full_err, void* workspace,
+                       uint64_t workspace_bytes, void* stream) {
+    if (rows <= 0 || cols <= 0 || samples <= 0) {
+        set_error("weights and calibration must be non-empty");
+        return EBX_ERR_INVALID;
+    }
+    if (!weights || !calib || !hw_err || !full_err) {
+        set_error("null argument");
+        return EBX_ERR_INVALID;
+    }
+    const uint64_t need = ebx_analyze_workspace_bytes(rows, samples);
+    if (!workspace || workspace_bytes < need) {
+        set_error("analyzer workspace missing or too small");
+        return EBX_ERR_WORKSPACE;
+    }
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    float* ref = reinterpret_cast<float*>(ws);
+    double* part = reinterpret_cast<double*>(
+        ws + ebx::round_up(uint64_t(rows) * uint64_t(samples) * 4, 256));
+    EBX_CUDA(ebx::launch_analyze(weights, rows, cols, calib, samples, ref, part, hw_err, full_err,
+                                 static_cast<cudaStream_t>(stream)));
+    return EBX_OK;
+}
+
+ebx_status ebx_quantize(const float* weights, int32_t rows, int32_t cols, int32_t bits,
+                        int16_t* codes, float* scales, void* stream) {
+    ebx_status st = validate_shape(rows, cols, bits, false);
+    if (st != EBX_OK) return st;
+    if (!weights || !codes || !scales) {
+        set_error("null argument");
+        return EBX_ERR_INVALID;
+    }
+    EBX_CUDA(ebx::launch_quantize(weights, rows, cols, bits, codes, scales,
+                                  static_cast<cudaStream_t>(stream)));
+    return EBX_OK;
+}
+
+ebx_status ebx_weights_to_fp16(const float* weights, int64_t n, void* out, void* stream) {
+    if (n < 0 || (n > 0 && (!weights || !out))) {
+        set_error("null argument");
+        return EBX_ERR_INVALID;
+    }
+    if (n == 0) return EBX_OK;
+    EBX_CUDA(ebx::launch_to_fp16(weights, n, static_cast<uint16_t*>(out),
+                                 static_cast<cudaStream_t>(stream)));
+    return EBX_OK;
+}
+
+ebx_status ebx_elastic_linear_packed(const void* x, int32_t x_dtype, int64_t rows,
+                                     const uint8_t* packed, const void* scales,
+                                     int32_t scale_dtype, const void* bias, int32_t bits,
+                                     int64_t group_size, int64_t out_features,
+                                     int64_t in_features, void* out, void* stream) {
+    if (bits < 2 || bits > 8) {
+        set_error("bits must be in [2,8]");
+        return EBX_ERR_INVALID;
+    }
+    if (group_size <= 0 || out_features <= 0 || in_features <= 0) {
+        set_error("invalid ElasticBit dimensions");
+        return EBX_ERR_INVALID;
+    }
+    if (x_dtype < 0 || x_dtype > 2 || scale_dtype < 0 || scale_dtype > 2) {
+        set_error("unsupported dtype code");
+        return EBX_ERR_INVALID;
+    }
+    if (rows < 0 || (rows > 0 && (!x || !packed || !scales || !out))) {
+        set_error("null argument");
+        return EBX_ERR_INVALID;
+    }
+    if (rows == 0) return EBX_OK;
+    EBX_CUDA(ebx::launch_elastic_linear_packed(x, x_dtype, rows, packed, scales, scale_dtype, bias,
+                                               bits, group_size, out_features, in_features, out,
+                                               static_cast<cudaStream_t>(stream)));
+    return EBX_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,153 @@
+// ebx_common.cuh -- shared definitions for the B200 ElasticBit runtime (libebx).
+//
+// Device execution layout ("tile layout")
+// ---------------------------------------
+// Storage stays the reference's MLB4 code: b-bit codes q+qmax (b = 3..15) or
+// raw fp16 (b = 16), one fp32 scale per row (elasticbit_runtime.cu:83-238).
+// On the device the same codes are kept at exactly b bits per weight, but
+// permuted so that one warp can stream them with 128-bit loads and decode them
+// straight into mma.m16n8k16 A-fragments:
+//
+//   * rows are grouped by 16 ("row group" g), K by 64 ("k-tile" t);
+//     N and K are padded up to 16 and 64 with q = 0 (decodes to +0.0);
+//   * one (g, t) supertile = 16 rows x 64 k = 1024 codes = b x 128 bytes,
+//     stored at ((g * KT) + t) * b * 128 (KT = Kp / 64): a row group's whole
+//     K-run is one contiguous byte range;
+//   * inside a supertile lane l owns 32 codes = b 32-bit words, packed LSB-first
+//     (code j at bits [j*b, j*b+b) of the lane's 32*b-bit little-endian word
+//     string).  The words are interleaved across lanes in vector segments so a
+//     warp loads them with coalesced 16-byte (then 8-, then 4-byte) accesses:
+//     seg s < b/4 holds words 4s..4s+3 at s*512 + l*16; if b%4 has bit 1, words
+//     4(b/4), +1 sit at (b/4)*512 + l*8; if b%4 has bit 0, the last word sits at
+//     (b/4)*512 + (b%4 >= 2 ? 256 : 0) + l*4;
+//   * code j = 8*s + e (s = MMA k-step 0..3, e = A-fragment element 0..7) holds
+//     the weight at  row = l/4 + 8*((e>>1)&1),
+//                    k   = 16*(l%4) + 4*s + 2*(e>>2) + (e&1).
+//     Matching B fragments then come from x[n][16*(l%4) .. 16*(l%4)+16), one
+//     32-byte run per token, because the same k permutation is applied to the
+//     activations (a dot product is invariant under a shared permutation of k).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ebx {
+
+constexpr int kRowGroup = 16;  // rows per supertile
+constexpr int kKTile = 64;     // k per supertile
+constexpr int kMinBits = 3;
+constexpr int kMaxBits = 15;
+constexpr int kFp16Bits = 16;
+
+__host__ __device__ constexpr int qmax_for(int bits) { return (1 << (bits - 1)) - 1; }
+__host__ __device__ constexpr int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+__host__ __device__ constexpr int64_t tile_bytes(int bits) { return int64_t(bits) * 128; }
+
+// Byte offset of word i of lane l inside one supertile of width `bits`.
+__host__ __device__ inline int word_offset(int bits, int lane, int i) {
+    const int nq = bits >> 2;
+    const int r = bits & 3;
+    if (i < 4 * nq) return (i >> 2) * 512 + lane * 16 + (i & 3) * 4;
+    int base = nq * 512;
+    if (r & 2) {
+        if (i < 4 * nq + 2) return base + lane * 8 + (i - 4 * nq) * 4;
+        base += 256;
+    }
+    return base + lane * 4;
+}
+
+// (row, k) inside the supertile of code j owned by lane l.
+__host__ __device__ inline void code_position(int lane, int j, int* row, int* k) {
+    const int s = j >> 3, e = j & 7;
+    *row = (lane >> 2) + 8 * ((e >> 1) & 1);
+    *k = 16 * (lane & 3) + 4 * s + 2 * (e >> 2) + (e & 1);
+}
+
+// ---------------------------------------------------------------------------
+// PTX helpers (sm_100a)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t pack2f(float lo, float hi) {
+    return (uint64_t(__float_as_uint(hi)) << 32) | uint64_t(__float_as_uint(lo));
+}
+
+// Exact decode of two codes to fp16: fp16_rn(fp32_rn((c - qmax) * s)).
+// `m0`, `m1` are the codes OR-ed into the mantissa of 2^23 (float 2^23 + c);
+// `neg_bias2` = (-(2^23 + qmax), same), `scale2` = (s, s).  The add is exact
+// (integers below 2^24), the multiply is one RN fp32 product like the
+// reference's `static_cast<float>(q) * scale`, and cvt.rn.f16x2 is the RN fp16
+// rounding of __float2half_rn.  Result: low half = first code.
+__device__ __forceinline__ uint32_t dequant2(uint32_t m0, uint32_t m1, uint64_t neg_bias2,
+                                             uint64_t scale2) {
+    uint32_t h;
+    asm("{\n\t.reg .b64 a, r;\n\t.reg .f32 lo, hi;\n\t"
+        "mov.b64 a, {%1, %2};\n\t"
+        "add.rn.f32x2 r, a, %3;\n\t"
+        "mul.rn.f32x2 r, r, %4;\n\t"
+        "mov.b64 {lo, hi}, r;\n\t"
+        "cvt.rn.f16x2.f32 %0, hi, lo;\n\t}"
+        : "=r"(h)
+        : "r"(m0), "r"(m1), "l"(neg_bias2), "l"(scale2));
+    return h;
+}
+
+// Integer codes as fp16 (no scale): used by the hardwareNative integer-dot
+// semantics, where the row scale is applied after accumulation.
+__device__ __forceinline__ uint32_t codes2_to_half(uint32_t m0, uint32_t m1, uint64_t neg_bias2) {
+    uint32_t h;
+    asm("{\n\t.reg .b64 a, r;\n\t.reg .f32 lo, hi;\n\t"
+        "mov.b64 a, {%1, %2};\n\t"
+        "add.rn.f32x2 r, a, %3;\n\t"
+        "mov.b64 {lo, hi}, r;\n\t"
+        "cvt.rn.f16x2.f32 %0, hi, lo;\n\t}"
+        : "=r"(h)
+        : "r"(m0), "r"(m1), "l"(neg_bias2));
+    return h;
+}
+
+// Code j of a lane-slice held in registers w[0..B-1], OR-ed into the mantissa
+// of 2^23 (the float 2^23 + code).  With B a compile-time constant and j an
+// unrolled index, the word index and shift fold to constants: one funnel or
+// plain shift (none when the code sits at bit 0) plus one LOP3.
+template <int B>
+__device__ __forceinline__ uint32_t code_magic(const uint32_t (&w)[B], int j) {
+    const int bit = j * B, wi = bit >> 5, o = bit & 31;
+    uint32_t v;
+    if (o == 0) v = w[wi];
+    else if (o + B <= 32) v = w[wi] >> o;
+    else v = __funnelshift_r(w[wi], w[wi + 1], o);
+    return (v & ((1u << B) - 1u)) | 0x4B000000u;
+}
+
+// D += A(16x16 fp16, row) * B(16x8 fp16, col), fp32 accumulate.
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                          uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// 16/8/4-byte async global->shared copies; src_bytes < size zero-fills.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global.L2::128B [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src),
+                 "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(dst), "l"(src));
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(dst), "l"(src));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+}  // namespace ebx

@@ -1,0 +1,57 @@
+// ebx_internal.h -- launchers shared between the libebx translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace ebx {
+
+struct Matrix {
+    int rows = 0;
+    int cols = 0;
+    int bits = 16;
+    int device = 0;
+    int exec_width = 16;       // 16: fp16(q*s) operands; 8/4: integer codes, scale after
+    int64_t kt = 0;            // k-tiles (Kp / 64)
+    int64_t groups = 0;        // row groups (Np / 16)
+    uint8_t* tiles = nullptr;  // groups * kt * bits * 128 bytes
+    size_t tiles_bytes = 0;
+    float* scales = nullptr;   // rows fp32 (null for 16-bit storage)
+};
+
+void set_error(const std::string& msg);
+
+// ebx_pack.cu ---------------------------------------------------------------
+// All return cudaError_t of the launch; `bad` (device int, may be null)
+// receives 1 if a code is outside [-qmax, qmax].
+cudaError_t launch_codes_to_tiles(const Matrix& m, const int16_t* codes, int* bad,
+                                  cudaStream_t s);
+cudaError_t launch_payload_to_tiles(const Matrix& m, const uint8_t* payload,
+                                    uint64_t payload_bytes, cudaStream_t s);
+cudaError_t launch_fp16_to_tiles(const Matrix& m, const uint16_t* w, cudaStream_t s);
+cudaError_t launch_tiles_to_payload(const Matrix& m, uint8_t* payload, uint64_t payload_bytes,
+                                    cudaStream_t s);
+cudaError_t launch_materialize(const Matrix& m, uint16_t* out, cudaStream_t s);
+
+// ebx_decode.cu -------------------------------------------------------------
+cudaError_t launch_decode(const Matrix& m, const uint16_t* x, int64_t M, const uint16_t* bias,
+                          uint16_t* y, float* y32, cudaStream_t s);
+
+// ebx_analyze.cu ------------------------------------------------------------
+cudaError_t launch_analyze(const float* w, int rows, int cols, const float* x, int samples,
+                           float* ref_scratch, double* part_scratch, double* hw, double* full,
+                           cudaStream_t s);
+cudaError_t launch_quantize(const float* w, int rows, int cols, int bits, int16_t* codes,
+                            float* scales, cudaStream_t s);
+cudaError_t launch_to_fp16(const float* w, int64_t n, uint16_t* out, cudaStream_t s);
+
+// ebx_packed_op.cu -----------------------------------------------------------
+cudaError_t launch_elastic_linear_packed(const void* x, int x_dtype, int64_t rows,
+                                         const uint8_t* packed, const void* scales,
+                                         int scale_dtype, const void* bias, int bits,
+                                         int64_t group_size, int64_t out_features,
+                                         int64_t in_features, void* out, cudaStream_t s);
+
+}  // namespace ebx

@@ -1,0 +1,76 @@
+"""Build recipes for the parity checker (test infrastructure only).
+
+* ``build_oracle()`` compiles ``oracle/ebx_oracle.c`` with gcc into
+  ``oracle/_build/libebx_oracle.so``.  ``-ffp-contract=off`` keeps float
+  products and sums un-fused, matching the reference host analyzer.
+* ``build_reference()`` compiles the reference's own ElasticBit runtime
+  (``mlbricks/elasticbit/csrc/elasticbit_runtime.cu`` in the MLBricks tree) out
+  of tree into ``oracle/_ref/_C.so`` with the same flags the reference's
+  setup.py gives it (``--use_fast_math``), for sm_100a.  It is only used as a
+  checker: its host analyzer produces the golden vectors in tests/golden, and
+  on a GPU box its RuntimeMatrix is an A/B reference.  The reference sources are
+  read in place and never copied.
+"""
+from __future__ import annotations
+
+import hashlib
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+BUILD_DIR = HERE / "_build"
+REF_DIR = HERE / "_ref"
+ORACLE_SO = BUILD_DIR / "libebx_oracle.so"
+REFERENCE_ROOT = Path(os.environ.get("EBX_REFERENCE_ROOT", "/root/reference"))
+REFERENCE_CU = REFERENCE_ROOT / "mlbricks" / "elasticbit" / "csrc" / "elasticbit_runtime.cu"
+
+
+def build_oracle(force: bool = False) -> Path:
+    src = HERE / "ebx_oracle.c"
+    BUILD_DIR.mkdir(exist_ok=True)
+    if not force and ORACLE_SO.exists() and ORACLE_SO.stat().st_mtime >= src.stat().st_mtime:
+        return ORACLE_SO
+    cmd = [
+        "gcc", "-O2", "-std=c11", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-shared",
+        str(src), "-o", str(ORACLE_SO), "-lm",
+    ]
+    subprocess.run(cmd, check=True)
+    return ORACLE_SO
+
+
+def build_reference(force: bool = False, verbose: bool = False) -> Path | None:
+    """Compile the reference ElasticBit runtime into oracle/_ref/_C.so.
+
+    Returns the path, or None when the reference tree is absent (GPU box).
+    Skips the ~3 minute nvcc build when the output matches the source hash.
+    """
+    out = REF_DIR / "_C.so"
+    if not REFERENCE_CU.exists():
+        return out if out.exists() else None
+    digest = hashlib.sha256(REFERENCE_CU.read_bytes()).hexdigest()
+    stamp = REF_DIR / "source.sha256"
+    if not force and out.exists() and stamp.exists() and stamp.read_text().strip() == digest:
+        return out
+    REF_DIR.mkdir(exist_ok=True)
+    from torch.utils.cpp_extension import load
+
+    load(
+        name="_C",
+        sources=[str(REFERENCE_CU)],
+        build_directory=str(REF_DIR),
+        extra_cflags=["-O3"],
+        extra_cuda_cflags=["-O3", "--use_fast_math",
+                           "-gencode", "arch=compute_100a,code=sm_100a"],
+        verbose=verbose,
+        is_python_module=True,
+    )
+    stamp.write_text(digest + "\n")
+    return out
+
+
+if __name__ == "__main__":
+    print(build_oracle(force="--force" in sys.argv))
+    if "--reference" in sys.argv:
+        print(build_reference(force="--force" in sys.argv, verbose=True))
