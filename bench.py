@@ -203,17 +203,22 @@ def run_gpu(args) -> None:
                 launch(M, e)
     stream.synchronize()
 
-    # one step captured as a CUDA graph with an event pair around every launch
+    # one CUDA graph per M holding its 9 launches; a step replays the 5 graphs.
+    # Events between graph replays (recorded on the launching stream) time each
+    # group of 9 launches; the host enqueues replays far faster than the GPU
+    # drains them, so no idle gap falls inside an event pair.
     nL = len(launches)
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(nL)]
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        for i, (M, e) in enumerate(launches):
-            ev[i][0].record(stream)
-            launch(M, e)
-            ev[i][1].record(stream)
-    for _ in range(max(args.warmup, 3)):
-        graph.replay()
+    graphs = {}
+    for M in MS:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for e in mats:
+                launch(M, e)
+        graphs[M] = g
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            for M in MS:
+                graphs[M].replay()
     stream.synchronize()
 
     sampler = ClockSampler(local)
@@ -224,16 +229,20 @@ def run_gpu(args) -> None:
     torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
-    per_launch = [0.0] * nL
-    t0.record(stream)
-    for _ in range(args.steps):
-        graph.replay()
-    t1.record(stream)
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            for _ in MS] for _ in range(args.steps)]
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for st in range(args.steps):
+            for j, M in enumerate(MS):
+                evs[st][j][0].record(stream)
+                graphs[M].replay()
+                evs[st][j][1].record(stream)
+        t1.record(stream)
     stream.synchronize()
     total_ms = t0.elapsed_time(t1)
-    # the graph's internal events hold the last replay's per-launch times
-    for i in range(nL):
-        per_launch[i] = ev[i][0].elapsed_time(ev[i][1])
+    m_ms = {M: sum(evs[st][j][0].elapsed_time(evs[st][j][1]) for st in range(args.steps))
+            for j, M in enumerate(MS)}
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -246,17 +255,15 @@ def run_gpu(args) -> None:
     ms_per_step = max_ms / args.steps
     value = step_bytes * world * args.steps / (max_ms * 1e-3) / 1e9
 
-    # roofline of the decode kernel: algorithmic bytes / summed launch durations
-    kern_ms = sum(per_launch)
-    achieved = step_bytes / (kern_ms * 1e-3) / 1e9
+    # roofline of the decode kernel: algorithmic bytes / device time of the
+    # launches (event pairs around each M group, summed over the timed steps)
+    kern_ms = sum(m_ms.values())
+    achieved = step_bytes * args.steps / (kern_ms * 1e-3) / 1e9
     pk = peaks()
-    by_m = {}
-    for i, (M, e) in enumerate(launches):
-        b = algorithmic_bytes(e["N"], e["K"], e["bits"], M)
-        by_m.setdefault(M, [0, 0.0])
-        by_m[M][0] += b
-        by_m[M][1] += per_launch[i]
-    per_m = {str(M): round(v[0] / (v[1] * 1e-3) / 1e9, 1) for M, v in by_m.items()}
+    per_m = {}
+    for M in MS:
+        b = sum(algorithmic_bytes(e["N"], e["K"], e["bits"], M) for e in mats) * args.steps
+        per_m[str(M)] = round(b / (m_ms[M] * 1e-3) / 1e9, 1)
 
     # e2e through the public API with pinned host buffers
     e2e = run_e2e(mats, device, args)
@@ -296,7 +303,7 @@ def run_gpu(args) -> None:
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
-    del graph
+    del graphs
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -405,8 +412,47 @@ def run_reference(args) -> None:
     }))
 
 
+def run_single(args) -> None:
+    """One (K, N, M) launch shape over a ring of `copies` compressed matrices
+    (for ncu captures of a small case: e.g. 3 x 4096x14336 at 10 bits = 220 MB,
+    above the 126 MB L2)."""
+    import ctypes
+
+    import torch
+
+    from mlbricks_b200 import _ebx
+    from mlbricks_b200.elasticbit.core import RuntimeMatrix, _selectBitsTorch
+
+    K, N, M = (int(v) for v in args.single.split(","))
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    lib = _ebx.load()
+    import numpy as np
+
+    mats = []
+    for i in range(args.copies):
+        w16 = baseline_weights_gpu(N, K, 7 + i, device)
+        calib = np.random.default_rng(i).standard_normal((32, K)).astype(np.float32)
+        bits, err, codes, scales = _selectBitsTorch(w16, calib, args.threshold)
+        mats.append(RuntimeMatrix._compressSelectedCodes(codes, scales, bits, args.threshold, err))
+        del w16, codes, scales
+    x = torch.randn((M, K), device=device, dtype=torch.float16)
+    y = torch.empty((M, N), device=device, dtype=torch.float16)
+    sptr = _ebx.stream_ptr()
+    for _ in range(args.warmup + args.steps):
+        for m in mats:
+            _ebx.check(lib.ebx_linear(ctypes.c_void_p(m._native.handle), x.data_ptr(), M, None,
+                                      y.data_ptr(), None, None, 0, sptr))
+    torch.cuda.synchronize()
+    print(json.dumps({"single": [K, N, M], "bits": [m.storageBits for m in mats],
+                      "launches": len(mats) * (args.warmup + args.steps)}))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
+    ap.add_argument("--single", default=None, help="K,N,M: one launch shape (profiling)")
+    ap.add_argument("--copies", type=int, default=3)
+    ap.add_argument("--threshold", type=float, default=0.01)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
@@ -414,7 +460,9 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.single:
+        run_single(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_gpu(args)

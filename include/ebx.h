@@ -148,6 +148,12 @@ EBX_API ebx_status ebx_quantize(const float* weights, int32_t rows, int32_t cols
  * (the 16-bit storage of pack_exact_weights, cu:113-120). */
 EBX_API ebx_status ebx_weights_to_fp16(const float* weights, int64_t n, void* out, void* stream);
 
+/* Device health word of `device`: 0 = healthy, nonzero = a kernel's bounded
+ * wait on a TMA copy gave up (the kernel then returned early; its outputs are
+ * unspecified).  `clear` = 1 resets it.  Synchronizes the device's legacy
+ * stream.  No reference counterpart: the reference kernels never wait. */
+EBX_API ebx_status ebx_device_status(int32_t device, int32_t* status, int32_t clear);
+
 /* FNV-1a 64 of a HOST byte range: the MLB4 scale/payload checksum
  * (elasticbit_runtime.cu:682-690, written at cu:1036-1037, checked at
  * cu:857-863). */

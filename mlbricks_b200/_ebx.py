@@ -63,6 +63,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ebx_analyze": (_ST, [_P, _I32, _I32, _P, _I32, _P, _P, _P, _U64, _P]),
     "ebx_quantize": (_ST, [_P, _I32, _I32, _I32, _P, _P, _P]),
     "ebx_weights_to_fp16": (_ST, [_P, _I64, _P, _P]),
+    "ebx_device_status": (_ST, [_I32, ctypes.POINTER(_I32), _I32]),
     "ebx_fnv1a64": (_U64, [_P, _U64]),
     "ebx_elastic_linear_packed": (
         _ST, [_P, _I32, _I64, _P, _P, _I32, _P, _I32, _I64, _I64, _I64, _P, _P]),

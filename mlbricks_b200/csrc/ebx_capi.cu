@@ -334,6 +334,19 @@ ebx_status ebx_linear(const ebx_matrix* h, const void* x, int64_t M, const void*
     return EBX_OK;
 }
 
+ebx_status ebx_device_status(int32_t device, int32_t* status, int32_t clear) {
+    if (!status) {
+        set_error("null argument");
+        return EBX_ERR_INVALID;
+    }
+    DeviceGuard g(device);
+    if (!g.ok) return cuda_fail(cudaErrorInvalidDevice, "cudaSetDevice");
+    int v = 0;
+    EBX_CUDA(ebx::read_device_status(&v, clear != 0, nullptr));
+    *status = v;
+    return EBX_OK;
+}
+
 uint64_t ebx_fnv1a64(const void* data, uint64_t size) {
     const uint8_t* p = static_cast<const uint8_t*>(data);
     uint64_t h = 1469598103934665603ull;

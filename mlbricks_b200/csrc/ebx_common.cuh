@@ -119,6 +119,86 @@ __device__ __forceinline__ uint32_t code_magic(const uint32_t (&w)[B], int j) {
     return (v & ((1u << B) - 1u)) | 0x4B000000u;
 }
 
+// Shifted code word: code j moved to bit 0 (upper bits still hold the next
+// codes; the LOP3 in dequant2_lop masks them).  No shift for a code at bit 0.
+template <int B>
+__device__ __forceinline__ uint32_t code_word(const uint32_t (&w)[B], int j) {
+    const int bit = j * B, wi = bit >> 5, o = bit & 31;
+    if (o == 0) return w[wi];
+    if (o + B <= 32) return w[wi] >> o;
+    return __funnelshift_r(w[wi], w[wi + 1], o);
+}
+
+// Exact decode of two shifted code words to fp16x2 in one asm block: LOP3
+// ((v & mask) | 2^23 magic, register operands), f32x2 add of -(2^23 + qmax),
+// f32x2 RN multiply by the row scale, cvt.rn.f16x2.  Same arithmetic as
+// dequant2; written as one block so the pair lives in one register pair.
+__device__ __forceinline__ uint32_t dequant2_lop(uint32_t v0, uint32_t v1, uint32_t mask,
+                                                 uint32_t magic, uint64_t neg_bias2,
+                                                 uint64_t scale2) {
+    uint32_t h;
+    asm("{\n\t.reg .b32 c0, c1;\n\t.reg .b64 a;\n\t"
+        "lop3.b32 c0, %1, %3, %4, 0xEA;\n\t"
+        "lop3.b32 c1, %2, %3, %4, 0xEA;\n\t"
+        "mov.b64 a, {c0, c1};\n\t"
+        "add.rn.f32x2 a, a, %5;\n\t"
+        "mul.rn.f32x2 a, a, %6;\n\t"
+        "mov.b64 {c0, c1}, a;\n\t"
+        "cvt.rn.f16x2.f32 %0, c1, c0;\n\t}"
+        : "=r"(h)
+        : "r"(v0), "r"(v1), "r"(mask), "r"(magic), "l"(neg_bias2), "l"(scale2));
+    return h;
+}
+
+// Integer codes to fp16x2 (no scale), for the scale-after-accumulation path.
+__device__ __forceinline__ uint32_t codes2_lop(uint32_t v0, uint32_t v1, uint32_t mask,
+                                               uint32_t magic, uint64_t neg_bias2) {
+    uint32_t h;
+    asm("{\n\t.reg .b32 c0, c1;\n\t.reg .b64 a;\n\t"
+        "lop3.b32 c0, %1, %3, %4, 0xEA;\n\t"
+        "lop3.b32 c1, %2, %3, %4, 0xEA;\n\t"
+        "mov.b64 a, {c0, c1};\n\t"
+        "add.rn.f32x2 a, a, %5;\n\t"
+        "mov.b64 {c0, c1}, a;\n\t"
+        "cvt.rn.f16x2.f32 %0, c1, c0;\n\t}"
+        : "=r"(h)
+        : "r"(v0), "r"(v1), "r"(mask), "r"(magic), "l"(neg_bias2));
+    return h;
+}
+
+// --- mbarrier + TMA bulk copy (non-tensor, no multicast) -------------------
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+// One bounded probe; returns true once the phase with parity `parity` completed.
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Global -> shared bulk copy completing on an mbarrier.  src/dst 16-byte
+// aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+
 // D += A(16x16 fp16, row) * B(16x8 fp16, col), fp32 accumulate.
 __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                           uint32_t b1) {

@@ -214,6 +214,197 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// v2: TMA-staged weight stream (the fast path; K % 8 == 0, x 16-byte aligned)
+// ---------------------------------------------------------------------------
+// Same CTA/warp mapping and arithmetic as decode_kernel, but each warp streams
+// its contiguous k-run of supertiles with cp.async.bulk (one instruction per
+// stage of ST supertiles, completing on a per-stage mbarrier) into a D-deep
+// shared-memory ring, and loads activations straight into registers one tile
+// ahead.  Every mbarrier wait is bounded: after kWaitLimit probes the warp
+// records EBX_DEVICE_TIMEOUT in g_device_status, drains its own copies (again
+// bounded) and leaves the loop, so a stuck copy cannot hang the GPU.
+__device__ int g_device_status = 0;
+constexpr int kDeviceTimeout = 0x7101;
+constexpr uint32_t kWaitLimit = 1u << 24;
+
+__device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity) {
+    for (uint32_t it = 0; it < kWaitLimit; ++it)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+template <int B, bool HW, int NT, int D, int ST>
+__global__ void __launch_bounds__(kThreads, 2) decode_tma_kernel(DecodeArgs a) {
+    constexpr int kTileBytes = B * 128;
+    constexpr int kStageBytes = ST * kTileBytes;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int g = blockIdx.x;
+    const int t0 = (warp * a.kt) / kWarps;
+    const int t1 = ((warp + 1) * a.kt) / kWarps;
+    const int nchunks = (t1 - t0 + ST - 1) / ST;
+    uint8_t* ring = smem + warp * D * kStageBytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * D * kStageBytes) + warp * D;
+    const uint8_t* gtiles = a.tiles + (size_t(g) * a.kt + t0) * kTileBytes;
+
+    if (lane == 0) {
+        for (int i = 0; i < D; ++i) mbar_init(smem_u32(&bars[i]), 1);
+        fence_proxy_async_smem();
+    }
+    __syncwarp();
+
+    auto issue = [&](int chunk) {  // lane 0 only
+        const int stage = chunk % D;
+        const int ntiles = min(ST, t1 - t0 - chunk * ST);
+        const uint32_t bytes = uint32_t(ntiles * kTileBytes);
+        const uint32_t bar = smem_u32(&bars[stage]);
+        mbar_expect_tx(bar, bytes);
+        bulk_g2s(smem_u32(ring + stage * kStageBytes), gtiles + size_t(chunk) * kStageBytes, bytes,
+                 bar);
+    };
+    if (lane == 0)
+        for (int c = 0; c < D && c < nchunks; ++c) issue(c);
+
+    const int r0 = lane >> 2;
+    const int c = lane & 3;
+    const int row_lo = g * kRowGroup + r0;
+    const int row_hi = row_lo + 8;
+    const uint32_t mask = (1u << B) - 1u;
+    const uint32_t magic = 0x4B000000u;
+    uint64_t nb2 = 0, slo2 = 0, shi2 = 0;
+    if constexpr (B != kFp16Bits) {
+        const float nb = -(8388608.0f + float(qmax_for(B)));
+        nb2 = pack2f(nb, nb);
+        if constexpr (!HW) {
+            const float sl = row_lo < a.N ? a.scales[row_lo] : 0.0f;
+            const float sh = row_hi < a.N ? a.scales[row_hi] : 0.0f;
+            slo2 = pack2f(sl, sl);
+            shi2 = pack2f(sh, sh);
+        }
+    }
+
+    // activation B-fragments: x[n][k0 + 16c .. +16) for n = r0 + 8nb
+    bool tok_ok[NT];
+    const uint16_t* xrow[NT];
+#pragma unroll
+    for (int nb = 0; nb < NT; ++nb) {
+        const int n = r0 + 8 * nb;
+        tok_ok[nb] = n < a.M;
+        xrow[nb] = a.x + size_t(tok_ok[nb] ? n : 0) * a.K + 16 * c;
+    }
+    auto load_x = [&](int t, uint32_t (&xb)[NT][8]) {
+#pragma unroll
+        for (int nb = 0; nb < NT; ++nb)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int k = t * kKTile + 16 * c + 8 * h;
+                uint4 v = make_uint4(0, 0, 0, 0);
+                if (tok_ok[nb] && k < a.K)
+                    v = __ldg(reinterpret_cast<const uint4*>(xrow[nb] + t * kKTile + 8 * h));
+                xb[nb][4 * h] = v.x; xb[nb][4 * h + 1] = v.y;
+                xb[nb][4 * h + 2] = v.z; xb[nb][4 * h + 3] = v.w;
+            }
+    };
+
+    float acc[NT][4];
+#pragma unroll
+    for (int nb = 0; nb < NT; ++nb)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[nb][i] = 0.0f;
+
+    uint32_t xcur[NT][8], xnext[NT][8];
+    if (t0 < t1) load_x(t0, xcur);
+    bool ok = true;
+    for (int chunk = 0; chunk < nchunks && ok; ++chunk) {
+        const int stage = chunk % D;
+        if (!bounded_wait(smem_u32(&bars[stage]), uint32_t((chunk / D) & 1))) {
+            ok = false;
+            break;
+        }
+        const int ntiles = min(ST, t1 - t0 - chunk * ST);
+        for (int tt = 0; tt < ntiles; ++tt) {
+            const int t = t0 + chunk * ST + tt;
+            const uint8_t* st = ring + stage * kStageBytes + tt * kTileBytes;
+            uint32_t w[B];
+#pragma unroll
+            for (int q = 0; q < B / 4; ++q) {
+                const uint4 v = *reinterpret_cast<const uint4*>(st + q * 512 + lane * 16);
+                w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
+            }
+            if constexpr ((B & 2) != 0) {
+                const uint2 v = *reinterpret_cast<const uint2*>(st + (B / 4) * 512 + lane * 8);
+                w[4 * (B / 4)] = v.x;
+                w[4 * (B / 4) + 1] = v.y;
+            }
+            if constexpr ((B & 1) != 0)
+                w[B - 1] = *reinterpret_cast<const uint32_t*>(st + (B / 4) * 512 +
+                                                              ((B & 2) ? 256 : 0) + lane * 4);
+            if (t + 1 < t1) load_x(t + 1, xnext);
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+                uint32_t af[4];
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const int p = 4 * s + r;
+                    if constexpr (B == kFp16Bits) {
+                        af[r] = w[p];
+                    } else if constexpr (HW) {
+                        af[r] = codes2_lop(code_word<B>(w, 2 * p), code_word<B>(w, 2 * p + 1), mask,
+                                           magic, nb2);
+                    } else {
+                        af[r] = dequant2_lop(code_word<B>(w, 2 * p), code_word<B>(w, 2 * p + 1),
+                                             mask, magic, nb2, (r & 1) ? shi2 : slo2);
+                    }
+                }
+#pragma unroll
+                for (int nb = 0; nb < NT; ++nb)
+                    mma_16816(acc[nb], af, xcur[nb][(s >> 1) * 4 + (s & 1) * 2],
+                              xcur[nb][(s >> 1) * 4 + (s & 1) * 2 + 1]);
+            }
+#pragma unroll
+            for (int nb = 0; nb < NT; ++nb)
+#pragma unroll
+                for (int i = 0; i < 8; ++i) xcur[nb][i] = xnext[nb][i];
+        }
+        // every lane has read this stage; refill it with chunk + D
+        __syncwarp();
+        if (lane == 0 && chunk + D < nchunks) {
+            fence_proxy_async_smem();
+            issue(chunk + D);
+        }
+    }
+    if (!ok) {
+        if (lane == 0) atomicExch(&g_device_status, kDeviceTimeout);
+        // drain this warp's copies still in flight (bounded), then fall through
+        for (int chunk = 0; chunk < nchunks; ++chunk)
+            bounded_wait(smem_u32(&bars[chunk % D]), uint32_t((chunk / D) & 1));
+    }
+
+    __syncthreads();
+    float* red = reinterpret_cast<float*>(smem);
+#pragma unroll
+    for (int nb = 0; nb < NT; ++nb)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) red[((warp * NT + nb) * 32 + lane) * 4 + i] = acc[nb][i];
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < NT * 128; idx += kThreads) {
+        const int nb = idx >> 7, l = (idx >> 2) & 31, i = idx & 3;
+        float v = 0.0f;
+#pragma unroll
+        for (int ww = 0; ww < kWarps; ++ww) v += red[((ww * NT + nb) * 32 + l) * 4 + i];
+        const int row = g * kRowGroup + (l >> 2) + 8 * (i >> 1);
+        const int tok = 8 * nb + (l & 3) * 2 + (i & 1);
+        if (row < a.N && tok < a.M) {
+            if constexpr (HW && B != kFp16Bits) v = v * a.scales[row];
+            if (a.bias) v += __half2float(__ushort_as_half(a.bias[row]));
+            a.y[size_t(tok) * a.N + row] = __half_as_ushort(__float2half_rn(v));
+            if (a.y32) a.y32[size_t(tok) * a.N + row] = v;
+        }
+    }
+}
+
 constexpr int kStages = 4;
 
 template <int B, bool HW, int NT, bool VECX>
@@ -238,14 +429,48 @@ cudaError_t launch_one(const DecodeArgs& a, int groups, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+template <int B, bool HW, int NT>
+cudaError_t launch_tma(const DecodeArgs& a, int groups, cudaStream_t s) {
+    constexpr int ST = B <= 12 ? 2 : 1;
+    constexpr int D = 4;
+    constexpr int ring = kWarps * D * ST * B * 128 + kWarps * D * 8;
+    constexpr int red = kWarps * NT * 128 * 4;
+    constexpr int smem = ring > red ? ring : red;
+    auto kern = decode_tma_kernel<B, HW, NT, D, ST>;
+    static std::atomic<uint64_t> configured{0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(configured.load(std::memory_order_relaxed) & bit)) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        configured.fetch_or(bit);
+    }
+    kern<<<groups, kThreads, smem, s>>>(a);
+    return cudaGetLastError();
+}
+
 template <int B, bool HW>
 cudaError_t dispatch_nt(const DecodeArgs& a, int groups, bool vecx, cudaStream_t s) {
-    if (a.M <= 8)
-        return vecx ? launch_one<B, HW, 1, true>(a, groups, s) : launch_one<B, HW, 1, false>(a, groups, s);
-    return vecx ? launch_one<B, HW, 2, true>(a, groups, s) : launch_one<B, HW, 2, false>(a, groups, s);
+    if (vecx)
+        return a.M <= 8 ? launch_tma<B, HW, 1>(a, groups, s) : launch_tma<B, HW, 2>(a, groups, s);
+    return a.M <= 8 ? launch_one<B, HW, 1, false>(a, groups, s) : launch_one<B, HW, 2, false>(a, groups, s);
 }
 
 }  // namespace
+
+cudaError_t read_device_status(int* status, bool clear, cudaStream_t s) {
+    cudaError_t e = cudaMemcpyFromSymbolAsync(status, g_device_status, sizeof(int), 0,
+                                              cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e == cudaSuccess && clear) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbolAsync(g_device_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    }
+    return e;
+}
 
 cudaError_t launch_decode(const Matrix& m, const uint16_t* x, int64_t M, const uint16_t* bias,
                           uint16_t* y, float* y32, cudaStream_t s) {

@@ -38,6 +38,9 @@ cudaError_t launch_materialize(const Matrix& m, uint16_t* out, cudaStream_t s);
 // ebx_decode.cu -------------------------------------------------------------
 cudaError_t launch_decode(const Matrix& m, const uint16_t* x, int64_t M, const uint16_t* bias,
                           uint16_t* y, float* y32, cudaStream_t s);
+// Reads (and optionally clears) the device-side status word that bounded
+// waits set on timeout (0 = healthy).  Synchronizes `s`.
+cudaError_t read_device_status(int* status, bool clear, cudaStream_t s);
 
 // ebx_analyze.cu ------------------------------------------------------------
 cudaError_t launch_analyze(const float* w, int rows, int cols, const float* x, int samples,

@@ -166,7 +166,9 @@ def test_config1_backends_agree(cuda_ok):
     assert ref_model[0].matrix.storageBits == nat_model[0].matrix.storageBits
     y_ref = ref_model(x).float().cpu().numpy()
     y_nat = nat_model(x).float().cpu().numpy()
+    # north_star bar: relative L2 <= 1e-3, max-abs <= 2e-3 (or one fp16 ulp of
+    # the value where that is larger: both routes round an fp32 sum to fp16)
     rel = np.linalg.norm(y_nat - y_ref) / np.linalg.norm(y_ref)
     assert rel <= 1e-3
-    ulp = np.abs(np.spacing(y_ref.astype(np.float16))).astype(np.float32)
-    assert np.all(np.abs(y_nat - y_ref) <= ulp)
+    ulp = np.spacing(np.abs(y_ref.astype(np.float16))).astype(np.float32)
+    assert np.all(np.abs(y_nat - y_ref) <= np.maximum(2e-3, ulp))
