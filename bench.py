@@ -438,20 +438,43 @@ def run_single(args) -> None:
         del w16, codes, scales
     x = torch.randn((M, K), device=device, dtype=torch.float16)
     y = torch.empty((M, N), device=device, dtype=torch.float16)
-    sptr = _ebx.stream_ptr()
-    for _ in range(args.warmup + args.steps):
+
+    def ring():
+        sp = _ebx.stream_ptr()  # the capture stream inside torch.cuda.graph
         for m in mats:
             _ebx.check(lib.ebx_linear(ctypes.c_void_p(m._native.handle), x.data_ptr(), M, None,
-                                      y.data_ptr(), None, None, 0, sptr))
+                                      y.data_ptr(), None, None, 0, sp))
+
+    for _ in range(args.warmup + args.steps):
+        ring()
     torch.cuda.synchronize()
-    print(json.dumps({"single": [K, N, M], "bits": [m.storageBits for m in mats],
-                      "launches": len(mats) * (args.warmup + args.steps)}))
+    out = {"single": [K, N, M], "bits": [m.storageBits for m in mats],
+           "launches": len(mats) * (args.warmup + args.steps)}
+    if args.time_single:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            ring()
+        g.replay()
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        reps = 50
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        b.record()
+        b.synchronize()
+        us = a.elapsed_time(b) * 1e3 / (reps * len(mats))
+        byts = sum(algorithmic_bytes(N, K, m.storageBits, M) for m in mats) / len(mats)
+        out.update({"us_per_launch": round(us, 3), "GBps": round(byts / (us * 1e-6) / 1e9, 1)})
+    print(json.dumps(out))
 
 
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--single", default=None, help="K,N,M: one launch shape (profiling)")
     ap.add_argument("--copies", type=int, default=3)
+    ap.add_argument("--time-single", action="store_true")
     ap.add_argument("--threshold", type=float, default=0.01)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)

@@ -14,7 +14,12 @@ from __future__ import annotations
 import ctypes
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libebx.so"
+import os
+
+# EBX_LIBRARY points at an alternative build of the same ABI (e.g. a variant
+# compiled with different kernel options); default: the in-tree build.
+LIB_PATH = Path(os.environ.get("EBX_LIBRARY") or
+                Path(__file__).resolve().parent / "_lib" / "libebx.so")
 
 EBX_OK = 0
 EBX_ERR_INVALID = 1

@@ -6,10 +6,12 @@
 // the host: the device holds only the exact-width tile codes and fp32 scales.
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <new>
 #include <string>
+#include <vector>
 
 #include "../../include/ebx.h"
 #include "ebx_common.cuh"
@@ -102,6 +104,21 @@ ebx_status alloc_matrix(int rows, int cols, int bits, int device, ebx_matrix** o
     return EBX_OK;
 }
 
+// Host check of the scales for the in-place decode path (see Matrix::direct_ok).
+cudaError_t check_scales(ebx::Matrix& m, cudaStream_t s) {
+    m.direct_ok = false;
+    if (!m.scales) return cudaSuccess;
+    std::vector<float> host(size_t(m.rows));
+    cudaError_t e = cudaMemcpyAsync(host.data(), m.scales, sizeof(float) * host.size(),
+                                    cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return e;
+    bool ok = true;
+    for (float v : host) ok = ok && std::isfinite(v) && std::fabs(v) >= 0x1p-100f;
+    m.direct_ok = ok;
+    return cudaSuccess;
+}
+
 void free_matrix(ebx_matrix* h) {
     if (!h) return;
     DeviceGuard g(h->m.device);
@@ -153,6 +170,7 @@ ebx_status ebx_matrix_create_from_codes(const int16_t* codes, const float* scale
     if (e == cudaSuccess) e = cudaMemcpyAsync(&bad_host, bad, sizeof(int), cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (bad) cudaFree(bad);
+    if (e == cudaSuccess) e = check_scales(h->m, s);
     if (e != cudaSuccess) {
         free_matrix(h);
         return cuda_fail(e, "ebx_matrix_create_from_codes");
@@ -204,6 +222,7 @@ ebx_status ebx_matrix_create_from_payload(const void* payload, uint64_t payload_
                        : ebx::launch_payload_to_tiles(h->m, dpay, payload_bytes, s);
     }
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e == cudaSuccess) e = check_scales(h->m, s);
     if (staged) cudaFree(staged);
     if (e != cudaSuccess) {
         free_matrix(h);

@@ -150,6 +150,24 @@ __device__ __forceinline__ uint32_t dequant2_lop(uint32_t v0, uint32_t v1, uint3
     return h;
 }
 
+// Scalar formulation of dequant2_lop (two LOP3, two FADD, two FMUL, one cvt):
+// identical results, no register-pair packing.
+__device__ __forceinline__ uint32_t dequant2_scalar(uint32_t v0, uint32_t v1, uint32_t mask,
+                                                    uint32_t magic, float neg_bias, float scale) {
+    uint32_t h;
+    asm("{\n\t.reg .b32 c0, c1;\n\t"
+        "lop3.b32 c0, %1, %3, %4, 0xEA;\n\t"
+        "lop3.b32 c1, %2, %3, %4, 0xEA;\n\t"
+        "add.rn.f32 c0, c0, %5;\n\t"
+        "add.rn.f32 c1, c1, %5;\n\t"
+        "mul.rn.f32 c0, c0, %6;\n\t"
+        "mul.rn.f32 c1, c1, %6;\n\t"
+        "cvt.rn.f16x2.f32 %0, c1, c0;\n\t}"
+        : "=r"(h)
+        : "r"(v0), "r"(v1), "r"(mask), "r"(magic), "f"(neg_bias), "f"(scale));
+    return h;
+}
+
 // Integer codes to fp16x2 (no scale), for the scale-after-accumulation path.
 __device__ __forceinline__ uint32_t codes2_lop(uint32_t v0, uint32_t v1, uint32_t mask,
                                                uint32_t magic, uint64_t neg_bias2) {
@@ -228,6 +246,129 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+}  // namespace ebx
+
+namespace ebx {
+
+// ---------------------------------------------------------------------------
+// Compile-time decode plan for a lane's 32 codes of width B (3..15).
+// Code j occupies bits [o, o+B) of word j*B/32 at o = (j*B) % 32.  When
+// o + B <= 23 the code can be decoded *in place*: (w & (mask << o)) | 2^23 is
+// the float 2^23 + code * 2^o, so subtracting 2^23 + qmax * 2^o gives q * 2^o
+// exactly and multiplying by s * 2^-o gives fp32_rn(q * s) (a power-of-two
+// factor moves between the operands without changing the exact product).  Up
+// to kMaxSlots distinct in-place offsets get their own scale register; every
+// other code is first shifted down to bit 0.
+// ---------------------------------------------------------------------------
+constexpr int kMaxSlots = 8;
+
+struct CodePlan {
+    int shift_word;  // -1: in place; else word index to shift from
+    int o;           // bit offset within the word
+    int slot;        // scale slot (in place only), 0 = offset 0
+};
+
+constexpr CodePlan plan_code(int B, int j) {
+    const int bit = j * B, wi = bit >> 5, o = bit & 31;
+    if (o + B <= 23) {
+        // slot = rank of o among the distinct in-place offsets of codes 0..j
+        int offs[kMaxSlots] = {0, 0, 0, 0, 0, 0, 0, 0};
+        int n = 0;
+        for (int jj = 0; jj <= j; ++jj) {
+            const int oo = (jj * B) & 31;
+            if (oo + B > 23) continue;
+            bool seen = false;
+            for (int k = 0; k < n; ++k) seen = seen || offs[k] == oo;
+            if (!seen) {
+                if (n == kMaxSlots) {
+                    if (oo == o) return CodePlan{wi, o, -1};
+                    continue;
+                }
+                offs[n++] = oo;
+            }
+        }
+        for (int k = 0; k < n; ++k)
+            if (offs[k] == o) return CodePlan{-1, o, k};
+        return CodePlan{wi, o, -1};
+    }
+    return CodePlan{wi, o, -1};
+}
+
+constexpr int slot_offset(int B, int slot) {
+    int offs[kMaxSlots] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int n = 0;
+    for (int j = 0; j < 32; ++j) {
+        const int o = (j * B) & 31;
+        if (o + B > 23) continue;
+        bool seen = false;
+        for (int k = 0; k < n; ++k) seen = seen || offs[k] == o;
+        if (!seen && n < kMaxSlots) offs[n++] = o;
+    }
+    return slot < n ? offs[slot] : -1;
+}
+
+constexpr int slot_count(int B) {
+    int n = 0;
+    for (int k = 0; k < kMaxSlots; ++k) n += slot_offset(B, k) >= 0 ? 1 : 0;
+    return n;
+}
+
+// s * 2^-offset factor per slot, as compile-time float constants.
+template <int B, int K>
+struct SlotScale {
+    static constexpr int kOff = slot_offset(B, K) < 0 ? 0 : slot_offset(B, K);
+    static constexpr float kFactor = 1.0f / float(1u << kOff);
+};
+
+// q*2^o as float from a code word (in place) or a shifted word (o = 0).
+template <int B, int O>
+__device__ __forceinline__ float code_to_float(uint32_t word, uint32_t magic) {
+    constexpr uint32_t kMask = ((1u << B) - 1u) << O;
+    constexpr float kBias = -(8388608.0f + float(qmax_for(B)) * float(1u << O));
+    uint32_t v;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(v) : "r"(word), "n"(kMask), "r"(magic));
+    return __fadd_rn(__uint_as_float(v), kBias);
+}
+
+// Code j of the lane slice -> fp32 q*s exactly rounded (before the fp16 cvt).
+// `sc` holds s * 2^-offset for each slot; sc[0] = s.
+template <int B, int J, bool DIRECT>
+__device__ __forceinline__ float decode_code(const uint32_t (&w)[B], const float (&sc)[kMaxSlots],
+                                             uint32_t magic) {
+    constexpr CodePlan p = plan_code(B, J);
+    if constexpr (DIRECT && p.shift_word < 0) {
+        return __fmul_rn(code_to_float<B, p.o>(w[(J * B) >> 5], magic), sc[p.slot]);
+    } else {
+        constexpr int bit = J * B, wi = bit >> 5, o = bit & 31;
+        uint32_t v;
+        if constexpr (o == 0) v = w[wi];
+        else if constexpr (o + B <= 32) v = w[wi] >> o;
+        else v = __funnelshift_r(w[wi], w[wi + 1], o);
+        return __fmul_rn(code_to_float<B, 0>(v, magic), sc[0]);
+    }
+}
+
+// Integer-code variant (scale applied after accumulation): exact q as float.
+template <int B, int J>
+__device__ __forceinline__ float decode_code_int(const uint32_t (&w)[B], uint32_t magic) {
+    constexpr int bit = J * B, wi = bit >> 5, o = bit & 31;
+    uint32_t v;
+    if constexpr (o == 0) v = w[wi];
+    else if constexpr (o + B <= 32) v = w[wi] >> o;
+    else v = __funnelshift_r(w[wi], w[wi + 1], o);
+    return code_to_float<B, 0>(v, magic);
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+    uint32_t h;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(hi), "f"(lo));
+    return h;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
 }
 
 }  // namespace ebx

@@ -42,6 +42,8 @@ struct DecodeArgs {
     float* y32;
     int M, N, K;
     int kt;
+    int groups;       // row groups (N padded to 16) / 16
+    uint32_t magic;   // 0x4B000000 (2^23), passed in so the compiler keeps it in a register
 };
 
 template <int B, int NT, bool VECX>
@@ -234,169 +236,225 @@ __device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity) {
     return false;
 }
 
-template <int B, bool HW, int NT, int D, int ST>
-__global__ void __launch_bounds__(kThreads, 2) decode_tma_kernel(DecodeArgs a) {
-    constexpr int kTileBytes = B * 128;
-    constexpr int kStageBytes = ST * kTileBytes;
+// ---------------------------------------------------------------------------
+// v4: CTA-wide TMA pipeline (the fast path)
+// ---------------------------------------------------------------------------
+// One CTA = one 16-row group over the full K.  Warps 0..7 consume; warp 8
+// produces.  The k-tiles are processed in rounds of 8 (one per consumer warp:
+// warp w takes tile 8r + w), so a round's 8 supertiles form one contiguous
+// byte range -> ONE bulk copy, and the round's activation slice is one bulk
+// copy of up to 512 halves per token row (lanes < M of the producer warp).  A
+// D-deep ring of rounds is guarded by per-stage full (TMA transaction count)
+// and empty (8 consumer-warp arrivals) mbarriers; every wait is bounded.
+template <int B, int NT, int RG>
+struct PipeStage {
+    static constexpr int kTileBytes = B * 128;
+    static constexpr int kWBytes = kWarps * kTileBytes;        // one row group's round
+    static constexpr int kXStride = kWarps * kKTile * 2 + 16;  // 1040 B: bank-shifted rows
+    static constexpr int kXBytes = NT * 8 * kXStride;
+    static constexpr int kBytes = RG * kWBytes + kXBytes;
+    static constexpr int kRedBytes = RG * kWarps * NT * 128 * 4;
+};
+
+// RG row groups per CTA (consumer warp w: row group w / 8, tile 8r + w % 8);
+// every consumer of a round reads the same activation slice, so activation
+// traffic per weight falls by RG.  Requires K % 64 == 0 (the generic kernel
+// covers the rest); activation rows of tokens >= M are zeroed once and never
+// written by the copy engine, so the fragment loads need no predicates.
+template <int B, bool HW, int NT, int D, bool DIRECT, int RG>
+__global__ void __launch_bounds__(kThreads * RG + 32, 1) decode_pipe_kernel(DecodeArgs a) {
+    using S = PipeStage<B, NT, RG>;
+    constexpr int kConsumers = kWarps * RG;
     extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + D * S::kBytes);
+    uint64_t* empty = full + D;
+    float* red = reinterpret_cast<float*>(empty + D);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int g = blockIdx.x;
-    const int t0 = (warp * a.kt) / kWarps;
-    const int t1 = ((warp + 1) * a.kt) / kWarps;
-    const int nchunks = (t1 - t0 + ST - 1) / ST;
-    uint8_t* ring = smem + warp * D * kStageBytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * D * kStageBytes) + warp * D;
-    const uint8_t* gtiles = a.tiles + (size_t(g) * a.kt + t0) * kTileBytes;
+    const int rounds = (a.kt + kWarps - 1) / kWarps;
+    const int mrows = a.M < NT * 8 ? a.M : NT * 8;
 
-    if (lane == 0) {
-        for (int i = 0; i < D; ++i) mbar_init(smem_u32(&bars[i]), 1);
-        fence_proxy_async_smem();
-    }
-    __syncwarp();
-
-    auto issue = [&](int chunk) {  // lane 0 only
-        const int stage = chunk % D;
-        const int ntiles = min(ST, t1 - t0 - chunk * ST);
-        const uint32_t bytes = uint32_t(ntiles * kTileBytes);
-        const uint32_t bar = smem_u32(&bars[stage]);
-        mbar_expect_tx(bar, bytes);
-        bulk_g2s(smem_u32(ring + stage * kStageBytes), gtiles + size_t(chunk) * kStageBytes, bytes,
-                 bar);
-    };
-    if (lane == 0)
-        for (int c = 0; c < D && c < nchunks; ++c) issue(c);
-
-    const int r0 = lane >> 2;
-    const int c = lane & 3;
-    const int row_lo = g * kRowGroup + r0;
-    const int row_hi = row_lo + 8;
-    const uint32_t mask = (1u << B) - 1u;
-    const uint32_t magic = 0x4B000000u;
-    uint64_t nb2 = 0, slo2 = 0, shi2 = 0;
-    if constexpr (B != kFp16Bits) {
-        const float nb = -(8388608.0f + float(qmax_for(B)));
-        nb2 = pack2f(nb, nb);
-        if constexpr (!HW) {
-            const float sl = row_lo < a.N ? a.scales[row_lo] : 0.0f;
-            const float sh = row_hi < a.N ? a.scales[row_hi] : 0.0f;
-            slo2 = pack2f(sl, sl);
-            shi2 = pack2f(sh, sh);
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < D; ++i) {
+            mbar_init(smem_u32(&full[i]), 1);
+            mbar_init(smem_u32(&empty[i]), kConsumers);
         }
     }
-
-    // activation B-fragments: x[n][k0 + 16c .. +16) for n = r0 + 8nb
-    bool tok_ok[NT];
-    const uint16_t* xrow[NT];
-#pragma unroll
-    for (int nb = 0; nb < NT; ++nb) {
-        const int n = r0 + 8 * nb;
-        tok_ok[nb] = n < a.M;
-        xrow[nb] = a.x + size_t(tok_ok[nb] ? n : 0) * a.K + 16 * c;
+    // zero the activation rows the copy engine never fills (tokens >= M)
+    for (int i = threadIdx.x; i < D * NT * 8 * (S::kXStride / 16); i += blockDim.x) {
+        const int st = i / (NT * 8 * (S::kXStride / 16));
+        const int rem = i % (NT * 8 * (S::kXStride / 16));
+        const int row = rem / (S::kXStride / 16);
+        if (row >= mrows)
+            *reinterpret_cast<uint4*>(smem + st * S::kBytes + RG * S::kWBytes +
+                                      row * S::kXStride + (rem % (S::kXStride / 16)) * 16) =
+                make_uint4(0, 0, 0, 0);
     }
-    auto load_x = [&](int t, uint32_t (&xb)[NT][8]) {
+    fence_proxy_async_smem();
+    __syncthreads();
+
+    if (warp == kConsumers) {
+        // ---------------- producer warp ----------------
+        for (int r = 0; r < rounds; ++r) {
+            const int st = r % D;
+            if (r >= D && !bounded_wait(smem_u32(&empty[st]), uint32_t(((r / D) - 1) & 1))) {
+                if (lane == 0) atomicExch(&g_device_status, kDeviceTimeout);
+                break;
+            }
+            const int ntile = min(kWarps, a.kt - r * kWarps);
+            const uint32_t xbytes = uint32_t(ntile * kKTile * 2);
+            uint8_t* dst = smem + st * S::kBytes;
+            const uint32_t bar = smem_u32(&full[st]);
+            int ngroups = 0;
+#pragma unroll
+            for (int rg = 0; rg < RG; ++rg) ngroups += (blockIdx.x * RG + rg) < a.groups ? 1 : 0;
+            if (lane == 0) {
+                mbar_expect_tx(bar, uint32_t(ngroups * ntile * S::kTileBytes) + xbytes * uint32_t(mrows));
+#pragma unroll
+                for (int rg = 0; rg < RG; ++rg) {
+                    const int g = blockIdx.x * RG + rg;
+                    if (g < a.groups)
+                        bulk_g2s(smem_u32(dst + rg * S::kWBytes),
+                                 a.tiles + (size_t(g) * a.kt + size_t(r) * kWarps) * S::kTileBytes,
+                                 uint32_t(ntile * S::kTileBytes), bar);
+                }
+            }
+            __syncwarp();
+            if (lane < mrows)
+                bulk_g2s(smem_u32(dst + RG * S::kWBytes + lane * S::kXStride),
+                         a.x + size_t(lane) * a.K + size_t(r) * kWarps * kKTile, xbytes, bar);
+        }
+    } else {
+        // ---------------- consumer warps ----------------
+        const int rgl = warp / kWarps;   // local row group
+        const int wt = warp % kWarps;    // tile slot within the round
+        const int g = blockIdx.x * RG + rgl;
+        const bool grp_ok = g < a.groups;
+        const int r0 = lane >> 2;
+        const int c = lane & 3;
+        const int row_lo = g * kRowGroup + r0;
+        const uint32_t magic = a.magic;  // opaque: kept in a register, never re-materialised
+        float sc[2][kMaxSlots];
+        if constexpr (B != kFp16Bits && !HW) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int row = row_lo + 8 * h;
+                const float s = (grp_ok && row < a.N) ? a.scales[row] : 0.0f;
+                // s * 2^-o for each in-place offset (exact power-of-two scaling)
+                sc[h][0] = s * SlotScale<B, 0>::kFactor;
+                sc[h][1] = s * SlotScale<B, 1>::kFactor;
+                sc[h][2] = s * SlotScale<B, 2>::kFactor;
+                sc[h][3] = s * SlotScale<B, 3>::kFactor;
+                sc[h][4] = s * SlotScale<B, 4>::kFactor;
+                sc[h][5] = s * SlotScale<B, 5>::kFactor;
+                sc[h][6] = s * SlotScale<B, 6>::kFactor;
+                sc[h][7] = s * SlotScale<B, 7>::kFactor;
+            }
+        }
+        float acc[NT][4];
 #pragma unroll
         for (int nb = 0; nb < NT; ++nb)
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int k = t * kKTile + 16 * c + 8 * h;
-                uint4 v = make_uint4(0, 0, 0, 0);
-                if (tok_ok[nb] && k < a.K)
-                    v = __ldg(reinterpret_cast<const uint4*>(xrow[nb] + t * kKTile + 8 * h));
-                xb[nb][4 * h] = v.x; xb[nb][4 * h + 1] = v.y;
-                xb[nb][4 * h + 2] = v.z; xb[nb][4 * h + 3] = v.w;
+            for (int i = 0; i < 4; ++i) acc[nb][i] = 0.0f;
+        const uint8_t* xbase = smem + RG * S::kWBytes + r0 * S::kXStride + wt * kKTile * 2 + 32 * c;
+
+        for (int r = 0; r < rounds; ++r) {
+            const int st = r % D;
+            if (!bounded_wait(smem_u32(&full[st]), uint32_t((r / D) & 1))) {
+                if (lane == 0) atomicExch(&g_device_status, kDeviceTimeout);
+                break;
             }
-    };
-
-    float acc[NT][4];
-#pragma unroll
-    for (int nb = 0; nb < NT; ++nb)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[nb][i] = 0.0f;
-
-    uint32_t xcur[NT][8], xnext[NT][8];
-    if (t0 < t1) load_x(t0, xcur);
-    bool ok = true;
-    for (int chunk = 0; chunk < nchunks && ok; ++chunk) {
-        const int stage = chunk % D;
-        if (!bounded_wait(smem_u32(&bars[stage]), uint32_t((chunk / D) & 1))) {
-            ok = false;
-            break;
-        }
-        const int ntiles = min(ST, t1 - t0 - chunk * ST);
-        for (int tt = 0; tt < ntiles; ++tt) {
-            const int t = t0 + chunk * ST + tt;
-            const uint8_t* st = ring + stage * kStageBytes + tt * kTileBytes;
+            const bool have = grp_ok && (r * kWarps + wt < a.kt);
+            const uint8_t* sw = smem + st * S::kBytes + rgl * S::kWBytes + wt * S::kTileBytes;
             uint32_t w[B];
+            uint32_t xb[NT][8];
+            if (have) {
 #pragma unroll
-            for (int q = 0; q < B / 4; ++q) {
-                const uint4 v = *reinterpret_cast<const uint4*>(st + q * 512 + lane * 16);
-                w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
+                for (int q = 0; q < B / 4; ++q) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(sw + q * 512 + lane * 16);
+                    w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
+                }
+                if constexpr ((B & 2) != 0) {
+                    const uint2 v = *reinterpret_cast<const uint2*>(sw + (B / 4) * 512 + lane * 8);
+                    w[4 * (B / 4)] = v.x;
+                    w[4 * (B / 4) + 1] = v.y;
+                }
+                if constexpr ((B & 1) != 0)
+                    w[B - 1] = *reinterpret_cast<const uint32_t*>(sw + (B / 4) * 512 +
+                                                                  ((B & 2) ? 256 : 0) + lane * 4);
+#pragma unroll
+                for (int nb = 0; nb < NT; ++nb)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const uint4 v = *reinterpret_cast<const uint4*>(
+                            xbase + st * S::kBytes + nb * 8 * S::kXStride + 16 * h);
+                        xb[nb][4 * h] = v.x; xb[nb][4 * h + 1] = v.y;
+                        xb[nb][4 * h + 2] = v.z; xb[nb][4 * h + 3] = v.w;
+                    }
             }
-            if constexpr ((B & 2) != 0) {
-                const uint2 v = *reinterpret_cast<const uint2*>(st + (B / 4) * 512 + lane * 8);
-                w[4 * (B / 4)] = v.x;
-                w[4 * (B / 4) + 1] = v.y;
-            }
-            if constexpr ((B & 1) != 0)
-                w[B - 1] = *reinterpret_cast<const uint32_t*>(st + (B / 4) * 512 +
-                                                              ((B & 2) ? 256 : 0) + lane * 4);
-            if (t + 1 < t1) load_x(t + 1, xnext);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&empty[st]));
+            if (!have) continue;
 #pragma unroll
             for (int s = 0; s < 4; ++s) {
                 uint32_t af[4];
+                if constexpr (B == kFp16Bits) {
 #pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                    const int p = 4 * s + r;
-                    if constexpr (B == kFp16Bits) {
-                        af[r] = w[p];
-                    } else if constexpr (HW) {
-                        af[r] = codes2_lop(code_word<B>(w, 2 * p), code_word<B>(w, 2 * p + 1), mask,
-                                           magic, nb2);
-                    } else {
-                        af[r] = dequant2_lop(code_word<B>(w, 2 * p), code_word<B>(w, 2 * p + 1),
-                                             mask, magic, nb2, (r & 1) ? shi2 : slo2);
+                    for (int rr = 0; rr < 4; ++rr) af[rr] = w[4 * s + rr];
+                } else {
+                    // pair p = 4s + rr holds codes 2p, 2p+1; rr odd -> row r0+8
+#define EBX_PAIR(RR)                                                                               \
+    do {                                                                                           \
+        constexpr int J = 2 * (4 * S_ + RR);                                                       \
+        float lo, hi;                                                                              \
+        if constexpr (HW) {                                                                        \
+            lo = decode_code_int<B, J>(w, magic);                                                  \
+            hi = decode_code_int<B, J + 1>(w, magic);                                              \
+        } else {                                                                                   \
+            lo = decode_code<B, J, DIRECT>(w, sc[RR & 1], magic);                                  \
+            hi = decode_code<B, J + 1, DIRECT>(w, sc[RR & 1], magic);                              \
+        }                                                                                          \
+        af[RR] = pack_half2(lo, hi);                                                               \
+    } while (0)
+                    switch (s) {
+#define EBX_STEP(SS)                    \
+    case SS: {                          \
+        constexpr int S_ = SS;          \
+        EBX_PAIR(0);                    \
+        EBX_PAIR(1);                    \
+        EBX_PAIR(2);                    \
+        EBX_PAIR(3);                    \
+        break;                          \
+    }
+                        EBX_STEP(0) EBX_STEP(1) EBX_STEP(2) EBX_STEP(3)
+#undef EBX_STEP
+#undef EBX_PAIR
                     }
                 }
 #pragma unroll
                 for (int nb = 0; nb < NT; ++nb)
-                    mma_16816(acc[nb], af, xcur[nb][(s >> 1) * 4 + (s & 1) * 2],
-                              xcur[nb][(s >> 1) * 4 + (s & 1) * 2 + 1]);
+                    mma_16816(acc[nb], af, xb[nb][(s >> 1) * 4 + (s & 1) * 2],
+                              xb[nb][(s >> 1) * 4 + (s & 1) * 2 + 1]);
             }
-#pragma unroll
-            for (int nb = 0; nb < NT; ++nb)
-#pragma unroll
-                for (int i = 0; i < 8; ++i) xcur[nb][i] = xnext[nb][i];
         }
-        // every lane has read this stage; refill it with chunk + D
-        __syncwarp();
-        if (lane == 0 && chunk + D < nchunks) {
-            fence_proxy_async_smem();
-            issue(chunk + D);
-        }
-    }
-    if (!ok) {
-        if (lane == 0) atomicExch(&g_device_status, kDeviceTimeout);
-        // drain this warp's copies still in flight (bounded), then fall through
-        for (int chunk = 0; chunk < nchunks; ++chunk)
-            bounded_wait(smem_u32(&bars[chunk % D]), uint32_t((chunk / D) & 1));
-    }
-
-    __syncthreads();
-    float* red = reinterpret_cast<float*>(smem);
 #pragma unroll
-    for (int nb = 0; nb < NT; ++nb)
+        for (int nb = 0; nb < NT; ++nb)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) red[((warp * NT + nb) * 32 + lane) * 4 + i] = acc[nb][i];
+            for (int i = 0; i < 4; ++i)
+                red[(((rgl * kWarps + wt) * NT + nb) * 32 + lane) * 4 + i] = acc[nb][i];
+    }
     __syncthreads();
-    for (int idx = threadIdx.x; idx < NT * 128; idx += kThreads) {
-        const int nb = idx >> 7, l = (idx >> 2) & 31, i = idx & 3;
+    for (int idx = threadIdx.x; idx < RG * NT * 128; idx += blockDim.x) {
+        const int rgl = idx / (NT * 128);
+        const int rem = idx % (NT * 128);
+        const int nb = rem >> 7, l = (rem >> 2) & 31, i = rem & 3;
+        const int g = blockIdx.x * RG + rgl;
         float v = 0.0f;
 #pragma unroll
-        for (int ww = 0; ww < kWarps; ++ww) v += red[((ww * NT + nb) * 32 + l) * 4 + i];
+        for (int ww = 0; ww < kWarps; ++ww) v += red[(((rgl * kWarps + ww) * NT + nb) * 32 + l) * 4 + i];
         const int row = g * kRowGroup + (l >> 2) + 8 * (i >> 1);
         const int tok = 8 * nb + (l & 3) * 2 + (i & 1);
-        if (row < a.N && tok < a.M) {
+        if (g < a.groups && row < a.N && tok < a.M) {
             if constexpr (HW && B != kFp16Bits) v = v * a.scales[row];
             if (a.bias) v += __half2float(__ushort_as_half(a.bias[row]));
             a.y[size_t(tok) * a.N + row] = __half_as_ushort(__float2half_rn(v));
@@ -429,14 +487,16 @@ cudaError_t launch_one(const DecodeArgs& a, int groups, cudaStream_t s) {
     return cudaGetLastError();
 }
 
-template <int B, bool HW, int NT>
-cudaError_t launch_tma(const DecodeArgs& a, int groups, cudaStream_t s) {
-    constexpr int ST = B <= 12 ? 2 : 1;
-    constexpr int D = 4;
-    constexpr int ring = kWarps * D * ST * B * 128 + kWarps * D * 8;
-    constexpr int red = kWarps * NT * 128 * 4;
-    constexpr int smem = ring > red ? ring : red;
-    auto kern = decode_tma_kernel<B, HW, NT, D, ST>;
+template <int B, bool HW, int NT, bool DIRECT, int RG>
+cudaError_t launch_pipe(const DecodeArgs& a, int groups, cudaStream_t s) {
+    using S = PipeStage<B, NT, RG>;
+    // RG == 1: two CTAs per SM (<= 113 KB each); RG == 2: one CTA per SM
+    constexpr int kBudget = RG == 1 ? 112 * 1024 : 220 * 1024;
+    constexpr int kExtra = S::kRedBytes + 128;
+    constexpr int Dfit = (kBudget - kExtra) / S::kBytes;
+    constexpr int D = Dfit >= 6 ? 6 : (Dfit >= 2 ? Dfit : 2);
+    constexpr int smem = D * S::kBytes + 2 * D * 8 + S::kRedBytes;
+    auto kern = decode_pipe_kernel<B, HW, NT, D, DIRECT, RG>;
     static std::atomic<uint64_t> configured{0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -447,14 +507,23 @@ cudaError_t launch_tma(const DecodeArgs& a, int groups, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         configured.fetch_or(bit);
     }
-    kern<<<groups, kThreads, smem, s>>>(a);
+    kern<<<(groups + RG - 1) / RG, kThreads * RG + 32, smem, s>>>(a);
     return cudaGetLastError();
 }
 
 template <int B, bool HW>
-cudaError_t dispatch_nt(const DecodeArgs& a, int groups, bool vecx, cudaStream_t s) {
-    if (vecx)
-        return a.M <= 8 ? launch_tma<B, HW, 1>(a, groups, s) : launch_tma<B, HW, 2>(a, groups, s);
+cudaError_t dispatch_nt(const DecodeArgs& a, int groups, bool pipe, bool direct, cudaStream_t s) {
+    if (pipe) {
+        constexpr bool kCanDirect = !HW && B != kFp16Bits;
+        if (a.M <= 8) {
+            if constexpr (kCanDirect)
+                if (direct) return launch_pipe<B, HW, 1, true, 1>(a, groups, s);
+            return launch_pipe<B, HW, 1, false, 1>(a, groups, s);
+        }
+        if constexpr (kCanDirect)
+            if (direct) return launch_pipe<B, HW, 2, true, 2>(a, groups, s);
+        return launch_pipe<B, HW, 2, false, 2>(a, groups, s);
+    }
     return a.M <= 8 ? launch_one<B, HW, 1, false>(a, groups, s) : launch_one<B, HW, 2, false>(a, groups, s);
 }
 
@@ -475,7 +544,7 @@ cudaError_t read_device_status(int* status, bool clear, cudaStream_t s) {
 cudaError_t launch_decode(const Matrix& m, const uint16_t* x, int64_t M, const uint16_t* bias,
                           uint16_t* y, float* y32, cudaStream_t s) {
     if (M <= 0) return cudaSuccess;
-    const bool vecx = (m.cols % 8) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    const bool vecx = (m.cols % 64) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
     const bool hw = m.exec_width < 16 && m.bits <= 8;
     for (int64_t m0 = 0; m0 < M; m0 += 16) {
         DecodeArgs a;
@@ -489,20 +558,22 @@ cudaError_t launch_decode(const Matrix& m, const uint16_t* x, int64_t M, const u
         a.N = m.rows;
         a.K = m.cols;
         a.kt = int(m.kt);
+        a.groups = int(m.groups);
+        a.magic = 0x4B000000u;
         const int groups = int(m.groups);
         cudaError_t e = cudaErrorInvalidValue;
         const bool v = vecx && ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0);
         switch (m.bits) {
 #define EBX_DEC_CASE(BB)                                                                \
     case BB:                                                                            \
-        e = hw ? dispatch_nt<BB, true>(a, groups, v, s) : dispatch_nt<BB, false>(a, groups, v, s); \
+        e = hw ? dispatch_nt<BB, true>(a, groups, v, m.direct_ok, s) : dispatch_nt<BB, false>(a, groups, v, m.direct_ok, s); \
         break;
             EBX_DEC_CASE(3) EBX_DEC_CASE(4) EBX_DEC_CASE(5) EBX_DEC_CASE(6) EBX_DEC_CASE(7)
             EBX_DEC_CASE(8)
 #undef EBX_DEC_CASE
 #define EBX_DEC_CASE_FULL(BB) \
     case BB:                  \
-        e = dispatch_nt<BB, false>(a, groups, v, s); \
+        e = dispatch_nt<BB, false>(a, groups, v, m.direct_ok, s); \
         break;
             EBX_DEC_CASE_FULL(9) EBX_DEC_CASE_FULL(10) EBX_DEC_CASE_FULL(11)
             EBX_DEC_CASE_FULL(12) EBX_DEC_CASE_FULL(13) EBX_DEC_CASE_FULL(14)

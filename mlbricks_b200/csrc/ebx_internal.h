@@ -19,6 +19,9 @@ struct Matrix {
     uint8_t* tiles = nullptr;  // groups * kt * bits * 128 bytes
     size_t tiles_bytes = 0;
     float* scales = nullptr;   // rows fp32 (null for 16-bit storage)
+    // Every scale is a finite normal >= 2^-100, so the decode kernel may use
+    // exactly rescaled copies s * 2^-o (in-place code extraction).
+    bool direct_ok = false;
 };
 
 void set_error(const std::string& msg);
