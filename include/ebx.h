@@ -137,6 +137,23 @@ EBX_API ebx_status ebx_analyze(const float* weights, int32_t rows, int32_t cols,
                        int32_t samples, double* hw_err, double* full_err, void* workspace,
                        uint64_t workspace_bytes, void* stream);
 
+/* Allocation-free form of ebx_analyze, for callers that cannot allocate
+ * device memory (their memory belongs to a host framework's fixed pool with no
+ * workspace to hand out, or they must avoid the device synchronisation that
+ * cudaMalloc/cudaFree can cause).  No counterpart in the reference: its
+ * analyzer runs on the host.  Same inputs, outputs and results as
+ * ebx_analyze; the scratch is a fixed 8 MiB array inside the library that
+ * every GPU loading it keeps until the process exits, so the call needs
+ * 256-byte-rounded 4*rows*samples + 336*rows bytes <= 8 MiB (e.g. 8192 rows x
+ * 32 samples) and returns EBX_ERR_INVALID with a message beyond that.  The
+ * first call on a device looks up the array's device address (with that
+ * device current); make that first call before any stream capture.  All
+ * calls on a device share the array: calls whose kernels overlap on the GPU
+ * (different streams without ordering) race and give wrong results. */
+EBX_API ebx_status ebx_analyze_noalloc(const float* weights, int32_t rows, int32_t cols,
+                                       const float* calib, int32_t samples, double* hw_err,
+                                       double* full_err, void* stream);
+
 /* Quantise fp32 weights [rows, cols] (DEVICE) for width 3..15: per-row scale
  * max|w|/qmax (1 for a zero row) and codes clamp(rint(w/s), +-qmax), written
  * to codes (int16 DEVICE) and scales (fp32 DEVICE).  Replaces make_row_scales +

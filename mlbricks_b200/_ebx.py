@@ -66,6 +66,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ebx_linear": (_ST, [_P, _P, _I64, _P, _P, _P, _P, _U64, _P]),
     "ebx_analyze_workspace_bytes": (_U64, [_I32, _I32]),
     "ebx_analyze": (_ST, [_P, _I32, _I32, _P, _I32, _P, _P, _P, _U64, _P]),
+    "ebx_analyze_noalloc": (_ST, [_P, _I32, _I32, _P, _I32, _P, _P, _P]),
     "ebx_quantize": (_ST, [_P, _I32, _I32, _I32, _P, _P, _P]),
     "ebx_weights_to_fp16": (_ST, [_P, _I64, _P, _P]),
     "ebx_device_status": (_ST, [_I32, ctypes.POINTER(_I32), _I32]),

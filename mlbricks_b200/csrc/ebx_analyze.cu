@@ -14,6 +14,10 @@
 // Layout: one warp per (row, width); lane s handles calibration sample s
 // (samples are processed 32 at a time).  The width-16 pass is the fp16
 // reference itself (cu:280-309 equals the b = 16 branch of cu:339-344).
+#include <mutex>
+#include <string>
+
+#include "../../include/ebx.h"
 #include "ebx_common.cuh"
 #include "ebx_internal.h"
 
@@ -199,3 +203,82 @@ cudaError_t launch_to_fp16(const float* w, int64_t n, uint16_t* out, cudaStream_
 }
 
 }  // namespace ebx
+
+// ---------------------------------------------------------------------------
+// Allocation-free analyzer: the same kernels, scratch in a fixed device array.
+// ---------------------------------------------------------------------------
+// Some callers cannot allocate device memory: code running inside a host
+// framework whose device memory belongs to that framework's pooled allocator
+// (with a fixed budget and no workspace handed to plugins), or latency-bound
+// code that must never hit the implicit device synchronisation of
+// cudaMalloc/cudaFree.  ebx_analyze_noalloc serves them from one static array
+// that every GPU loading this library holds for the life of the process.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB per device
+static __device__ __align__(256) unsigned char g_analyze_scratch[kNoAllocScratchBytes];
+
+// In host code `g_analyze_scratch` names a host-side stand-in, not device
+// memory; the device address comes from cudaGetSymbolAddress, taken once per
+// device with that device current.
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[64] = {};
+
+cudaError_t noalloc_scratch(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_analyze_scratch);
+        if (e != cudaSuccess) return e;
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" ebx_status ebx_analyze_noalloc(const float* weights, int32_t rows, int32_t cols,
+                                          const float* calib, int32_t samples, double* hw_err,
+                                          double* full_err, void* stream) {
+    if (rows <= 0 || cols <= 0 || samples <= 0) {
+        ebx::set_error("weights and calibration must be non-empty");
+        return EBX_ERR_INVALID;
+    }
+    if (!weights || !calib || !hw_err || !full_err) {
+        ebx::set_error("null argument");
+        return EBX_ERR_INVALID;
+    }
+    // same layout as ebx_analyze's workspace: fp16 reference outputs, then the
+    // per-(width, row) squared-error sums
+    const uint64_t ref_bytes = ebx::round_up(uint64_t(rows) * uint64_t(samples) * 4, 256);
+    const uint64_t need = ref_bytes + uint64_t(rows) * 14 * 3 * 8;
+    if (need > kNoAllocScratchBytes) {
+        ebx::set_error("ebx_analyze_noalloc: " + std::to_string(rows) + " rows x " +
+                       std::to_string(samples) + " samples need " + std::to_string(need) +
+                       " bytes of scratch, more than the built-in " +
+                       std::to_string(kNoAllocScratchBytes) +
+                       "; use ebx_analyze with a caller workspace");
+        return EBX_ERR_INVALID;
+    }
+    void* base = nullptr;
+    cudaError_t e = noalloc_scratch(&base);
+    if (e == cudaSuccess) {
+        // Nothing needs zeroing: every reference value and every partial sum the
+        // finishing kernel reads is written earlier in this same call.
+        float* ref = static_cast<float*>(base);
+        double* part = reinterpret_cast<double*>(static_cast<unsigned char*>(base) + ref_bytes);
+        e = ebx::launch_analyze(weights, rows, cols, calib, samples, ref, part, hw_err, full_err,
+                                static_cast<cudaStream_t>(stream));
+    }
+    if (e != cudaSuccess) {
+        ebx::set_error(std::string("CUDA error: ") + cudaGetErrorString(e) +
+                       " in ebx_analyze_noalloc");
+        return EBX_ERR_CUDA;
+    }
+    return EBX_OK;
+}
