@@ -438,12 +438,14 @@ def run_single(args) -> None:
         del w16, codes, scales
     x = torch.randn((M, K), device=device, dtype=torch.float16)
     y = torch.empty((M, N), device=device, dtype=torch.float16)
+    nws = int(lib.ebx_linear_workspace_bytes(ctypes.c_void_p(mats[0]._native.handle), M))
+    ws = torch.empty(max(nws, 1), dtype=torch.uint8, device=device)
 
     def ring():
         sp = _ebx.stream_ptr()  # the capture stream inside torch.cuda.graph
         for m in mats:
             _ebx.check(lib.ebx_linear(ctypes.c_void_p(m._native.handle), x.data_ptr(), M, None,
-                                      y.data_ptr(), None, None, 0, sp))
+                                      y.data_ptr(), None, ws.data_ptr(), nws, sp))
 
     for _ in range(args.warmup + args.steps):
         ring()
@@ -466,7 +468,25 @@ def run_single(args) -> None:
         b.synchronize()
         us = a.elapsed_time(b) * 1e3 / (reps * len(mats))
         byts = sum(algorithmic_bytes(N, K, m.storageBits, M) for m in mats) / len(mats)
-        out.update({"us_per_launch": round(us, 3), "GBps": round(byts / (us * 1e-6) / 1e9, 1)})
+        out.update({"us_per_launch": round(us, 3), "GBps": round(byts / (us * 1e-6) / 1e9, 1),
+                    "TFLOPs": round(2.0 * M * N * K / (us * 1e-6) / 1e12, 1)})
+        if nws:
+            # the materialise step alone (exact fp16 weight into the workspace)
+            gm = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gm):
+                for m in mats:
+                    _ebx.check(lib.ebx_matrix_materialize(ctypes.c_void_p(m._native.handle),
+                                                          ws.data_ptr(), _ebx.stream_ptr()))
+            gm.replay()
+            torch.cuda.synchronize()
+            a.record()
+            for _ in range(reps):
+                gm.replay()
+            b.record()
+            b.synchronize()
+            mus = a.elapsed_time(b) * 1e3 / (reps * len(mats))
+            out.update({"materialize_us": round(mus, 3),
+                        "gemm_TFLOPs": round(2.0 * M * N * K / ((us - mus) * 1e-6) / 1e12, 1)})
     print(json.dumps(out))
 
 

@@ -327,15 +327,14 @@ ebx_status ebx_matrix_materialize(const ebx_matrix* h, void* dst, void* stream) 
 }
 
 uint64_t ebx_linear_workspace_bytes(const ebx_matrix* h, int64_t M) {
-    (void)h;
-    (void)M;
-    return 0;
+    // M > kGemmMinRows: room for the exactly dequantised fp16 weight fed to the
+    // tensor-core GEMM; smaller M runs the decode kernel and needs nothing.
+    if (!h || M <= ebx::kGemmMinRows || (h->m.cols % 8) != 0) return 0;
+    return uint64_t(ebx::round_up(int64_t(h->m.rows) * h->m.cols * 2, 256));
 }
 
 ebx_status ebx_linear(const ebx_matrix* h, const void* x, int64_t M, const void* bias, void* y,
                       float* y32, void* workspace, uint64_t workspace_bytes, void* stream) {
-    (void)workspace;
-    (void)workspace_bytes;
     if (!h || (M > 0 && (!x || !y))) {
         set_error("null argument");
         return EBX_ERR_INVALID;
@@ -347,6 +346,20 @@ ebx_status ebx_linear(const ebx_matrix* h, const void* x, int64_t M, const void*
     if (M == 0) return EBX_OK;
     DeviceGuard g(h->m.device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const uint64_t need = ebx_linear_workspace_bytes(h, M);
+    if (need > 0 && ebx::gemm_supported(h->m.cols, x, workspace)) {
+        // prefill: exact fp16 weight into the workspace, then the tcgen05 GEMM
+        if (workspace_bytes < need) {
+            set_error("ebx_linear: workspace missing or smaller than ebx_linear_workspace_bytes()");
+            return EBX_ERR_WORKSPACE;
+        }
+        uint16_t* w16 = static_cast<uint16_t*>(workspace);
+        EBX_CUDA(ebx::launch_materialize(h->m, w16, s));
+        EBX_CUDA(ebx::launch_gemm_f16(static_cast<const uint16_t*>(x), w16, M, h->m.rows,
+                                      h->m.cols, static_cast<const uint16_t*>(bias),
+                                      static_cast<uint16_t*>(y), y32, s));
+        return EBX_OK;
+    }
     EBX_CUDA(ebx::launch_decode(h->m, static_cast<const uint16_t*>(x), M,
                                 static_cast<const uint16_t*>(bias), static_cast<uint16_t*>(y), y32,
                                 s));
@@ -360,9 +373,10 @@ ebx_status ebx_device_status(int32_t device, int32_t* status, int32_t clear) {
     }
     DeviceGuard g(device);
     if (!g.ok) return cuda_fail(cudaErrorInvalidDevice, "cudaSetDevice");
-    int v = 0;
+    int v = 0, vg = 0;
     EBX_CUDA(ebx::read_device_status(&v, clear != 0, nullptr));
-    *status = v;
+    EBX_CUDA(ebx::read_gemm_status(&vg, clear != 0, nullptr));
+    *status = v ? v : vg;
     return EBX_OK;
 }
 

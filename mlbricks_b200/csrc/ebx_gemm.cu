@@ -1,0 +1,307 @@
+// ebx_gemm.cu -- prefill (M > 64) ElasticBit linear on B200 tensor cores.
+//
+// Replaces the reference's prefill route, materialise + cuBLAS F.linear
+// (core.py:465-471, elasticbit_runtime.cu:982-1022): the exactly dequantised
+// FP16 weight W16[n,k] = fp16(q * s) (the same bits the reference's
+// RuntimeMatrix holds for its W16 path) is written to the caller's workspace by
+// ebx_pack.cu's materialize kernel, then this kernel computes
+//     y[m, n] = fp16( sum_k x[m,k] * W16[n,k] + bias[n] )
+// with 5th-generation tensor cores:
+//   * CTA tile 128 (tokens, MMA M) x 256 (weight rows, MMA N), K step 64;
+//   * TMA (cp.async.bulk.tensor, 128-byte swizzle, no multicast) loads the
+//     x and W16 tiles into a 4-stage shared-memory ring;
+//   * one thread issues tcgen05.mma (kind::f16, fp32 accumulate) into a
+//     128 x 256 fp32 accumulator in tensor memory; tcgen05.commit frees each
+//     stage when the MMAs reading it complete;
+//   * four warps read the accumulator back with tcgen05.ld (warp w owns TMEM
+//     lanes 32w..32w+31 = tokens), add the bias in fp32 and store fp16 (+fp32).
+// Every mbarrier wait is bounded; a timeout sets the device status word.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <mutex>
+
+#include "ebx_common.cuh"
+#include "ebx_internal.h"
+
+namespace ebx {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int kStagesG = 4;
+constexpr int kABytes = BM * BK * 2;
+constexpr int kBBytes = BN * BK * 2;
+constexpr int kStageBytesG = kABytes + kBBytes;
+constexpr int kTmemCols = 256;
+constexpr int kGemmThreads = 128;
+constexpr uint32_t kGemmWaitLimit = 1u << 22;
+
+// instruction descriptor: D fp32, A/B fp16, both K-major, N = 256, M = 128
+constexpr uint32_t kIdesc = (1u << 4) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+
+__device__ int g_gemm_status = 0;
+
+struct GemmArgs {
+    const uint16_t* bias;
+    uint16_t* y;
+    float* y32;
+    int M, N, K;
+};
+
+// Shared-memory matrix descriptor: K-major tile with 128-byte swizzle, rows of
+// 128 bytes, 8-row core groups 1024 bytes apart (SBO), sm_100 version field.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = uint64_t((saddr & 0x3FFFFu) >> 4);
+    d |= uint64_t(1) << 16;            // leading byte offset (unused for swizzled K-major)
+    d |= uint64_t(1024 >> 4) << 32;    // stride byte offset
+    d |= uint64_t(1) << 46;            // descriptor version
+    d |= uint64_t(2) << 61;            // SWIZZLE_128B
+    return d;
+}
+
+__device__ __forceinline__ bool gemm_wait(uint32_t bar, uint32_t parity) {
+    for (uint32_t it = 0; it < kGemmWaitLimit; ++it)
+        if (mbar_try_wait(bar, parity)) return true;
+    atomicExch(&g_gemm_status, 0x7102);
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];\n" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem),
+        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)
+                 : "memory");
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_x, const __grid_constant__ CUtensorMap tma_w,
+                    GemmArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStagesG * kStageBytesG);
+    uint64_t* empty = full + kStagesG;
+    uint64_t* done = empty + kStagesG;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BN;
+    const int m0 = blockIdx.y * BM;
+    const int kblocks = (a.K + BK - 1) / BK;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int i = 0; i < kStagesG; ++i) {
+                mbar_init(smem_u32(&full[i]), 1);
+                mbar_init(smem_u32(&empty[i]), 1);
+            }
+            mbar_init(smem_u32(done), 1);
+            fence_proxy_async_smem();
+        }
+        __syncwarp();
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {  // TMA producer
+            for (int kb = 0; kb < kblocks; ++kb) {
+                const int st = kb % kStagesG;
+                if (kb >= kStagesG &&
+                    !gemm_wait(smem_u32(&empty[st]), uint32_t(((kb / kStagesG) - 1) & 1)))
+                    break;
+                const uint32_t bar = smem_u32(&full[st]);
+                mbar_expect_tx(bar, kStageBytesG);
+                uint8_t* stage = smem + st * kStageBytesG;
+                tma_load_2d(smem_u32(stage), &tma_x, kb * BK, m0, bar);
+                tma_load_2d(smem_u32(stage + kABytes), &tma_w, kb * BK, n0, bar);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issuer
+            bool ok = true;
+            for (int kb = 0; kb < kblocks && ok; ++kb) {
+                const int st = kb % kStagesG;
+                ok = gemm_wait(smem_u32(&full[st]), uint32_t((kb / kStagesG) & 1));
+                if (!ok) break;
+                asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+                const uint32_t abase = smem_u32(smem + st * kStageBytesG);
+                const uint32_t bbase = abase + kABytes;
+#pragma unroll
+                for (int k = 0; k < BK / 16; ++k)
+                    umma_f16(tmem, sw128_desc(abase + k * 32), sw128_desc(bbase + k * 32),
+                             (kb | k) != 0 ? 1u : 0u);
+                umma_commit(smem_u32(&empty[st]));
+            }
+            umma_commit(smem_u32(done));  // fires when every MMA above has completed
+        }
+        __syncwarp();
+    }
+
+    // ---------------- epilogue: TMEM -> registers -> global ----------------
+    const bool ready = gemm_wait(smem_u32(done), 0u);
+    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+    const int m = m0 + warp * 32 + lane;
+    const bool vec = (a.N % 8) == 0;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+        uint32_t v[32];
+        const uint32_t taddr = tmem + (uint32_t(warp * 32) << 16) + uint32_t(c * 32);
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+            "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+              "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
+              "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]),
+              "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+              "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]),
+              "=r"(v[31])
+            : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+        const int nb = n0 + c * 32;
+        if (!ready || m >= a.M || nb >= a.N) continue;
+        float f[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            f[j] = __uint_as_float(v[j]);
+            if (a.bias && nb + j < a.N) f[j] += __half2float(__ushort_as_half(a.bias[nb + j]));
+        }
+        uint16_t* yrow = a.y + size_t(m) * a.N + nb;
+        if (vec && nb + 32 <= a.N) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                uint4 pk;
+                pk.x = pack_half2(f[8 * q + 0], f[8 * q + 1]);
+                pk.y = pack_half2(f[8 * q + 2], f[8 * q + 3]);
+                pk.z = pack_half2(f[8 * q + 4], f[8 * q + 5]);
+                pk.w = pack_half2(f[8 * q + 6], f[8 * q + 7]);
+                reinterpret_cast<uint4*>(yrow)[q] = pk;
+            }
+            if (a.y32) {
+                float* y32row = a.y32 + size_t(m) * a.N + nb;
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    reinterpret_cast<float4*>(y32row)[q] =
+                        make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                if (nb + j < a.N) {
+                    yrow[j] = __half_as_ushort(__float2half_rn(f[j]));
+                    if (a.y32) a.y32[size_t(m) * a.N + nb + j] = f[j];
+                }
+            }
+        }
+    }
+
+    asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem),
+                     "r"(kTmemCols)
+                     : "memory");
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static std::once_flag once;
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// Row-major fp16 [rows, K] tensor map with a (64 x box_rows) box, 128 B swizzle.
+bool make_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(rows)};
+    const cuuint64_t strides[1] = {cuuint64_t(K) * 2};
+    const cuuint32_t box[2] = {cuuint32_t(BK), cuuint32_t(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+cudaError_t read_gemm_status(int* status, bool clear, cudaStream_t s) {
+    cudaError_t e = cudaMemcpyFromSymbolAsync(status, g_gemm_status, sizeof(int), 0,
+                                              cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e == cudaSuccess && clear) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbolAsync(g_gemm_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    }
+    return e;
+}
+
+bool gemm_supported(int K, const void* x, const void* w16) {
+    return (K % 8) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+           (reinterpret_cast<uintptr_t>(w16) & 15) == 0 && encode_fn() != nullptr;
+}
+
+cudaError_t launch_gemm_f16(const uint16_t* x, const uint16_t* w16, int64_t M, int N, int K,
+                            const uint16_t* bias, uint16_t* y, float* y32, cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    CUtensorMap tx, tw;
+    if (!make_map(&tx, x, int(M), K, BM) || !make_map(&tw, w16, N, K, BN))
+        return cudaErrorInvalidValue;
+    constexpr int smem = kStagesG * kStageBytesG + 1024 + 256;
+    static std::atomic<uint64_t> configured{0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(configured.load(std::memory_order_relaxed) & bit)) {
+        e = cudaFuncSetAttribute(gemm_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        configured.fetch_or(bit);
+    }
+    GemmArgs a{bias, y, y32, int(M), N, K};
+    dim3 grid(unsigned((N + BN - 1) / BN), unsigned((M + BM - 1) / BM));
+    gemm_f16_kernel<<<grid, kGemmThreads, smem, s>>>(tx, tw, a);
+    return cudaGetLastError();
+}
+
+}  // namespace ebx

@@ -45,6 +45,14 @@ cudaError_t launch_decode(const Matrix& m, const uint16_t* x, int64_t M, const u
 // waits set on timeout (0 = healthy).  Synchronizes `s`.
 cudaError_t read_device_status(int* status, bool clear, cudaStream_t s);
 
+// ebx_gemm.cu ---------------------------------------------------------------
+// Rows above which ebx_linear takes the materialise + tcgen05 GEMM route.
+constexpr int64_t kGemmMinRows = 64;
+bool gemm_supported(int K, const void* x, const void* w16);
+cudaError_t launch_gemm_f16(const uint16_t* x, const uint16_t* w16, int64_t M, int N, int K,
+                            const uint16_t* bias, uint16_t* y, float* y32, cudaStream_t s);
+cudaError_t read_gemm_status(int* status, bool clear, cudaStream_t s);
+
 // ebx_analyze.cu ------------------------------------------------------------
 cudaError_t launch_analyze(const float* w, int rows, int cols, const float* x, int samples,
                            float* ref_scratch, double* part_scratch, double* hw, double* full,

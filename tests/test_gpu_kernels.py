@@ -318,3 +318,32 @@ def test_device_status_healthy_after_all_kernels(lib):
     st = ctypes.c_int32(-1)
     _ebx.check(lib.ebx_device_status(0, ctypes.byref(st), 0))
     assert st.value == 0
+
+
+@pytest.mark.parametrize("M,rows,cols", [(65, 96, 512), (128, 256, 64), (300, 1000, 520),
+                                         (256, 1536, 384), (512, 4096, 4096), (200, 4096, 14336)])
+def test_prefill_gemm(lib, M, rows, cols):
+    """M > 64: exact fp16 weight materialised into the workspace, tcgen05 GEMM."""
+    bits = 10
+    w = O.baseline_weights(rows, cols, seed=M + rows)
+    s = O.row_scales(w, bits)
+    q = O.quantize(w, s, bits)
+    h = from_codes(lib, q, s, bits)
+    assert lib.ebx_linear_workspace_bytes(h.h, M) >= rows * cols * 2
+    x = O.normal((M, cols), seed=M).astype(np.float16)
+    bias = O.normal((rows,), seed=5, scale=0.1).astype(np.float16)
+    y16, y32 = linear(lib, h, x, rows, bias)
+    w16 = O.dequantize_codes(q, s).astype(np.float64)
+    ref = x.astype(np.float64) @ w16.T + bias.astype(np.float64)
+    assert_close_to_oracle(y16, y32, ref)
+    y16b, y32b = linear(lib, h, x, rows, bias)
+    assert np.array_equal(y32b, y32)  # deterministic
+
+
+def test_prefill_without_workspace_is_refused(lib):
+    q, s = random_codes(64, 128, 9, seed=2)
+    h = from_codes(lib, q, s, 9)
+    x = torch.zeros((100, 128), dtype=torch.float16, device=dev())
+    y = torch.empty((100, 64), dtype=torch.float16, device=dev())
+    st = lib.ebx_linear(h.h, x.data_ptr(), 100, None, y.data_ptr(), None, None, 0, stream())
+    assert st == _ebx.EBX_ERR_WORKSPACE
