@@ -265,6 +265,10 @@ def run_gpu(args) -> None:
         b = sum(algorithmic_bytes(e["N"], e["K"], e["bits"], M) for e in mats) * args.steps
         per_m[str(M)] = round(b / (m_ms[M] * 1e-3) / 1e9, 1)
 
+    # prefill sweep: M in {256, 1024, 4096} on the three shapes at
+    # threshold 0.01, through ebx_linear (exact fp16 materialise + tcgen05 GEMM)
+    prefill = run_prefill(mats, device, lib, args) if not args.no_prefill else None
+
     # e2e through the public API with pinned host buffers
     e2e = run_e2e(mats, device, args)
 
@@ -298,6 +302,7 @@ def run_gpu(args) -> None:
             "peak_source": pk["source"], "kernel": "ebx decode_kernel (M<=16)",
         },
         "e2e": e2e,
+        "prefill": prefill,
         "gpu_launches": nL * args.steps,
         "clocks": clocks,
     }
@@ -309,6 +314,62 @@ def run_gpu(args) -> None:
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(result))
+
+
+PREFILL_MS = [256, 1024, 4096]
+
+
+def run_prefill(mats, device, lib, args) -> dict:
+    """Time ebx_linear for M > 64 (materialise + tcgen05 GEMM); TFLOP/s = 2MNK / time.
+    Shapes are visited round-robin so each launch follows >126 MB of other traffic."""
+    import ctypes
+
+    import torch
+
+    from mlbricks_b200 import _ebx
+
+    sel = [e for e in mats if e["threshold"] == 0.01]
+    pk = peaks()
+    maxws = max(e["N"] * e["K"] * 2 for e in sel)
+    ws = torch.empty(maxws + 256, dtype=torch.uint8, device=device)
+    cases = []
+    for M in PREFILL_MS:
+        xs = {e["K"]: torch.randn((M, e["K"]), device=device, dtype=torch.float16) for e in sel}
+        ys = {e["N"]: torch.empty((M, e["N"]), device=device, dtype=torch.float16) for e in sel}
+        ms = {id(e): [] for e in sel}
+
+        def run(e):
+            h = ctypes.c_void_p(e["matrix"]._native.handle)
+            nws = int(lib.ebx_linear_workspace_bytes(h, M))
+            _ebx.check(lib.ebx_linear(h, xs[e["K"]].data_ptr(), M, None, ys[e["N"]].data_ptr(),
+                                      None, ws.data_ptr(), nws, _ebx.stream_ptr()))
+
+        for _ in range(2):
+            for e in sel:
+                run(e)
+        torch.cuda.synchronize()
+        for _ in range(max(3, min(args.steps, 10))):
+            for e in sel:
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record()
+                run(e)
+                b.record()
+                b.synchronize()
+                ms[id(e)].append(a.elapsed_time(b))
+        for e in sel:
+            t = statistics.median(ms[id(e)])
+            cases.append({"M": M, "K": e["K"], "N": e["N"], "bits": e["bits"], "ms": round(t, 4),
+                          "TFLOPs": round(2.0 * M * e["N"] * e["K"] / (t * 1e-3) / 1e12, 1)})
+    big = [c for c in cases if c["M"] == 4096]
+    agg = sum(2.0 * c["M"] * c["N"] * c["K"] for c in big) / (sum(c["ms"] for c in big) * 1e-3) / 1e12
+    return {"workload": "config3: M in {256,1024,4096} x (K,N) in {(4096,4096),(4096,14336),"
+                        "(14336,4096)}, threshold 0.01; ebx_linear = exact fp16 materialise + "
+                        "tcgen05 GEMM; median of timed launches",
+            "M4096_TFLOPs": round(agg, 1), "cases": cases,
+            "roofline": {"bound": "tensor", "achieved": round(agg, 1), "peak": pk["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": round(agg / pk["bf16_tflops"], 4),
+                         "peak_source": pk["source"] + " (bf16 dense burst; fp16 has the same rate)"}}
 
 
 def run_e2e(mats, device, args) -> dict:
@@ -502,6 +563,7 @@ def main() -> None:
     ap.add_argument("--impl", default="ebx", choices=["ebx", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
     args = ap.parse_args()
     if args.single:
         run_single(args)

@@ -44,6 +44,8 @@ struct DecodeArgs {
     int kt;
     int groups;       // row groups (N padded to 16) / 16
     uint32_t magic;   // 0x4B000000 (2^23), passed in so the compiler keeps it in a register
+    int stages;       // pipe kernel: ring depth (runtime, <= kMaxStages)
+    int stage_bytes;  // pipe kernel: RG weight rounds + (min(M, 8 NT) + 1) activation rows
 };
 
 template <int B, int NT, bool VECX>
@@ -246,14 +248,16 @@ __device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity) {
 // copy of up to 512 halves per token row (lanes < M of the producer warp).  A
 // D-deep ring of rounds is guarded by per-stage full (TMA transaction count)
 // and empty (8 consumer-warp arrivals) mbarriers; every wait is bounded.
+constexpr int kMaxStages = 8;
+
 template <int B, int NT, int RG>
 struct PipeStage {
     static constexpr int kTileBytes = B * 128;
     static constexpr int kWBytes = kWarps * kTileBytes;        // one row group's round
     static constexpr int kXStride = kWarps * kKTile * 2 + 16;  // 1040 B: bank-shifted rows
-    static constexpr int kXBytes = NT * 8 * kXStride;
-    static constexpr int kBytes = RG * kWBytes + kXBytes;
     static constexpr int kRedBytes = RG * kWarps * NT * 128 * 4;
+    // stage = RG weight rounds + activation rows of tokens 0..m-1 + one zero row
+    static int bytes(int m) { return RG * kWBytes + (m + 1) * kXStride; }
 };
 
 // RG row groups per CTA (consumer warp w: row group w / 8, tile 8r + w % 8);
@@ -261,14 +265,16 @@ struct PipeStage {
 // traffic per weight falls by RG.  Requires K % 64 == 0 (the generic kernel
 // covers the rest); activation rows of tokens >= M are zeroed once and never
 // written by the copy engine, so the fragment loads need no predicates.
-template <int B, bool HW, int NT, int D, bool DIRECT, int RG>
-__global__ void __launch_bounds__(kThreads * RG + 32, 1) decode_pipe_kernel(DecodeArgs a) {
+template <int B, bool HW, int NT, bool DIRECT, int RG, int MINB>
+__global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(DecodeArgs a) {
     using S = PipeStage<B, NT, RG>;
     constexpr int kConsumers = kWarps * RG;
     extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + D * S::kBytes);
-    uint64_t* empty = full + D;
-    float* red = reinterpret_cast<float*>(empty + D);
+    const int D = a.stages;
+    const int SB = a.stage_bytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + D * SB);
+    uint64_t* empty = full + kMaxStages;
+    float* red = reinterpret_cast<float*>(empty + kMaxStages);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int rounds = (a.kt + kWarps - 1) / kWarps;
@@ -280,30 +286,26 @@ __global__ void __launch_bounds__(kThreads * RG + 32, 1) decode_pipe_kernel(Deco
             mbar_init(smem_u32(&empty[i]), kConsumers);
         }
     }
-    // zero the activation rows the copy engine never fills (tokens >= M)
-    for (int i = threadIdx.x; i < D * NT * 8 * (S::kXStride / 16); i += blockDim.x) {
-        const int st = i / (NT * 8 * (S::kXStride / 16));
-        const int rem = i % (NT * 8 * (S::kXStride / 16));
-        const int row = rem / (S::kXStride / 16);
-        if (row >= mrows)
-            *reinterpret_cast<uint4*>(smem + st * S::kBytes + RG * S::kWBytes +
-                                      row * S::kXStride + (rem % (S::kXStride / 16)) * 16) =
-                make_uint4(0, 0, 0, 0);
-    }
+    // zero row (index mrows) of every stage, never written by the copy engine:
+    // lanes whose token is >= M read it
+    for (int i = threadIdx.x; i < D * (S::kXStride / 16); i += blockDim.x)
+        *reinterpret_cast<uint4*>(smem + (i / (S::kXStride / 16)) * SB + RG * S::kWBytes +
+                                  mrows * S::kXStride + (i % (S::kXStride / 16)) * 16) =
+            make_uint4(0, 0, 0, 0);
     fence_proxy_async_smem();
     __syncthreads();
 
     if (warp == kConsumers) {
         // ---------------- producer warp ----------------
-        for (int r = 0; r < rounds; ++r) {
-            const int st = r % D;
-            if (r >= D && !bounded_wait(smem_u32(&empty[st]), uint32_t(((r / D) - 1) & 1))) {
+        int st = 0, ph = 0;
+        for (int r = 0; r < rounds; ++r, st = (st + 1 == D ? 0 : st + 1), ph ^= (st == 0)) {
+            if (r >= D && !bounded_wait(smem_u32(&empty[st]), uint32_t(ph ^ 1))) {
                 if (lane == 0) atomicExch(&g_device_status, kDeviceTimeout);
                 break;
             }
             const int ntile = min(kWarps, a.kt - r * kWarps);
             const uint32_t xbytes = uint32_t(ntile * kKTile * 2);
-            uint8_t* dst = smem + st * S::kBytes;
+            uint8_t* dst = smem + st * SB;
             const uint32_t bar = smem_u32(&full[st]);
             int ngroups = 0;
 #pragma unroll
@@ -356,16 +358,23 @@ __global__ void __launch_bounds__(kThreads * RG + 32, 1) decode_pipe_kernel(Deco
         for (int nb = 0; nb < NT; ++nb)
 #pragma unroll
             for (int i = 0; i < 4; ++i) acc[nb][i] = 0.0f;
-        const uint8_t* xbase = smem + RG * S::kWBytes + r0 * S::kXStride + wt * kKTile * 2 + 32 * c;
+        // activation row of token r0 + 8 nb, or the zero row when that token >= M
+        const uint8_t* xrow[NT];
+#pragma unroll
+        for (int nb = 0; nb < NT; ++nb) {
+            const int tok = r0 + 8 * nb;
+            xrow[nb] = smem + RG * S::kWBytes + (tok < mrows ? tok : mrows) * S::kXStride +
+                       wt * kKTile * 2 + 32 * c;
+        }
 
-        for (int r = 0; r < rounds; ++r) {
-            const int st = r % D;
-            if (!bounded_wait(smem_u32(&full[st]), uint32_t((r / D) & 1))) {
+        int st = 0, ph = 0;
+        for (int r = 0; r < rounds; ++r, st = (st + 1 == D ? 0 : st + 1), ph ^= (st == 0)) {
+            if (!bounded_wait(smem_u32(&full[st]), uint32_t(ph))) {
                 if (lane == 0) atomicExch(&g_device_status, kDeviceTimeout);
                 break;
             }
             const bool have = grp_ok && (r * kWarps + wt < a.kt);
-            const uint8_t* sw = smem + st * S::kBytes + rgl * S::kWBytes + wt * S::kTileBytes;
+            const uint8_t* sw = smem + st * SB + rgl * S::kWBytes + wt * S::kTileBytes;
             uint32_t w[B];
             uint32_t xb[NT][8];
             if (have) {
@@ -386,8 +395,7 @@ __global__ void __launch_bounds__(kThreads * RG + 32, 1) decode_pipe_kernel(Deco
                 for (int nb = 0; nb < NT; ++nb)
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
-                        const uint4 v = *reinterpret_cast<const uint4*>(
-                            xbase + st * S::kBytes + nb * 8 * S::kXStride + 16 * h);
+                        const uint4 v = *reinterpret_cast<const uint4*>(xrow[nb] + st * SB + 16 * h);
                         xb[nb][4 * h] = v.x; xb[nb][4 * h + 1] = v.y;
                         xb[nb][4 * h + 2] = v.z; xb[nb][4 * h + 3] = v.w;
                     }
@@ -488,22 +496,27 @@ cudaError_t launch_one(const DecodeArgs& a, int groups, cudaStream_t s) {
 }
 
 template <int B, bool HW, int NT, bool DIRECT, int RG>
-cudaError_t launch_pipe(const DecodeArgs& a, int groups, cudaStream_t s) {
+cudaError_t launch_pipe(DecodeArgs a, int groups, cudaStream_t s) {
     using S = PipeStage<B, NT, RG>;
-    // RG == 1: two CTAs per SM (<= 113 KB each); RG == 2: one CTA per SM
-    constexpr int kBudget = RG == 1 ? 112 * 1024 : 220 * 1024;
-    constexpr int kExtra = S::kRedBytes + 128;
-    constexpr int Dfit = (kBudget - kExtra) / S::kBytes;
-    constexpr int D = Dfit >= 6 ? 6 : (Dfit >= 2 ? Dfit : 2);
-    constexpr int smem = D * S::kBytes + 2 * D * 8 + S::kRedBytes;
-    auto kern = decode_pipe_kernel<B, HW, NT, D, DIRECT, RG>;
+    // RG == 1: three CTAs per SM (27 warps); RG == 2: one CTA per SM.  The ring
+    // is as deep as that budget allows for this M (2..kMaxStages stages).
+    constexpr int MINB = RG == 1 ? 3 : 1;
+    constexpr int kBudget = RG == 1 ? 74 * 1024 : 215 * 1024;
+    constexpr int kFixed = 2 * kMaxStages * 8 + S::kRedBytes + 16;
+    const int mrows = a.M < NT * 8 ? a.M : NT * 8;
+    a.stage_bytes = S::bytes(mrows);
+    int D = (kBudget - kFixed) / a.stage_bytes;
+    D = D > kMaxStages ? kMaxStages : (D < 2 ? 2 : D);
+    a.stages = D;
+    const int smem = D * a.stage_bytes + kFixed;
+    auto kern = decode_pipe_kernel<B, HW, NT, DIRECT, RG, MINB>;
     static std::atomic<uint64_t> configured{0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     const uint64_t bit = 1ull << (dev & 63);
     if (!(configured.load(std::memory_order_relaxed) & bit)) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kBudget);
         if (e != cudaSuccess) return e;
         configured.fetch_or(bit);
     }
