@@ -272,6 +272,13 @@ def run_gpu(args) -> None:
     # e2e through the public API with pinned host buffers
     e2e = run_e2e(mats, device, args)
 
+    # config 5: tensor-parallel 8B-shaped linear stack over all ranks
+    mat_info = [{"K": e["K"], "N": e["N"], "threshold": e["threshold"], "bits": e["bits"]}
+                for e in mats]
+    del mats, handles, launches
+    torch.cuda.empty_cache()
+    tp_stack = None if args.no_tp_stack else run_tp_stack(args, world, rank, device)
+
     result = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -284,13 +291,12 @@ def run_gpu(args) -> None:
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "fp16 activations x b-bit codes (b=" +
-                 ",".join(str(b) for b in sorted({e["bits"] for e in mats})) + "), fp32 accumulate",
+                 ",".join(str(b) for b in sorted({e["bits"] for e in mat_info})) + "), fp32 accumulate",
         "data": "synthetic (BASELINE weight scheme, seeded; no dataset)",
         "config": {
             "workload": "config2 decode GEMV sweep: M in {1,2,4,8,16} x (K,N) in "
                         "{(4096,4096),(4096,14336),(14336,4096)} x threshold {0.005,0.01,0.02}",
-            "matrices": [{"K": e["K"], "N": e["N"], "threshold": e["threshold"], "bits": e["bits"]}
-                         for e in mats],
+            "matrices": mat_info,
             "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
             "l2": "inputs larger than L2: 9 matrices (~0.5 GB codes) visited round-robin",
             "timing": "CUDA graph of one step replayed; CUDA events on the launching stream",
@@ -303,6 +309,7 @@ def run_gpu(args) -> None:
         },
         "e2e": e2e,
         "prefill": prefill,
+        "tp_stack": tp_stack,
         "gpu_launches": nL * args.steps,
         "clocks": clocks,
     }
@@ -313,10 +320,150 @@ def run_gpu(args) -> None:
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
-        print(json.dumps(result))
+        emit(result)
 
 
 PREFILL_MS = [256, 1024, 4096]
+
+# 8B-shaped Llama linear stack, (name, K, N, tensor-parallel mode)
+STACK_LAYERS = 32
+STACK_MATS = [("qkv", 4096, 6144, "column"), ("o", 4096, 4096, "row"),
+              ("gate", 4096, 14336, "column"), ("up", 4096, 14336, "column"),
+              ("down", 14336, 4096, "row")]
+STACK_HEAD = ("lm_head", 4096, 128256, "column")
+
+
+def quantize_rows(w16, bits: int):
+    """Per-row scale max|w|/qmax and codes round(w/s) clamped -- the analyzer's
+    own quantisation step (same torch operations as _selectBitsTorch)."""
+    import torch
+
+    w32 = w16.float()
+    qm = float((1 << (bits - 1)) - 1)
+    mx = w32.abs().amax(dim=1)
+    sc = torch.where(mx > 0.0, mx / qm, torch.ones_like(mx))
+    q = torch.round(w32 / sc[:, None]).clamp(min=-qm, max=qm).to(torch.int16)
+    return q, sc
+
+
+def build_stack(device, world: int, rank: int, collectives):
+    """Compress the stack once per shape-class with the analyzer (threshold 0.01,
+    32 calibration rows), then quantise every layer's seeded weight at that width
+    and keep this rank's Megatron shard."""
+    import numpy as np
+    import torch
+
+    from mlbricks_b200.elasticbit import tensor_parallel as tp
+    from mlbricks_b200.elasticbit.core import _selectBitsTorch
+
+    bits_of = {}
+    for idx, (name, K, N, _) in enumerate(STACK_MATS + [STACK_HEAD]):
+        w = baseline_weights_gpu(N, K, 1000 + idx, device)
+        calib = np.random.default_rng(5).standard_normal((32, K)).astype(np.float32)
+        b, _, _, _ = _selectBitsTorch(w, calib, 0.01)
+        bits_of[name] = min(b, 15)
+        del w
+    layers = []
+    for li in range(STACK_LAYERS):
+        layer = {}
+        for mi, (name, K, N, mode) in enumerate(STACK_MATS):
+            w = baseline_weights_gpu(N, K, 10_000 + li * 16 + mi, device)
+            q, sc = quantize_rows(w, bits_of[name])
+            del w
+            layer[name] = tp.build_sharded(q, sc, bits_of[name], mode, world, rank,
+                                           collectives=collectives,
+                                           input_is_local=(mode == "row"))
+            del q, sc
+        layers.append(layer)
+    name, K, N, mode = STACK_HEAD
+    w = baseline_weights_gpu(N, K, 99_999, device)
+    q, sc = quantize_rows(w, bits_of[name])
+    del w
+    head = tp.build_sharded(q, sc, bits_of[name], mode, world, rank, collectives=collectives)
+    del q, sc
+    torch.cuda.empty_cache()
+    return layers, head, bits_of
+
+
+def stack_step(layers, head, h, world: int):
+    """One forward of the linear stack on M rows (attention replaced by the q slice of
+    QKV; SiLU(gate) * up between the MLP projections); returns local logits."""
+    import torch
+
+    for L in layers:
+        qkv = L["qkv"](h)                               # [M, 6144 / W] local
+        attn = qkv[:, : 4096 // world]                  # local heads -> O's K slice
+        h = L["o"](attn)                                # all-reduce -> [M, 4096]
+        g = L["gate"](h)
+        u = L["up"](h)
+        act = (torch.nn.functional.silu(g.float()) * u.float()).to(torch.float16)
+        h = L["down"](act)                              # all-reduce -> [M, 4096]
+    return head(h)
+
+
+def run_tp_stack(args, world: int, rank: int, device) -> dict:
+    import torch
+    import torch.distributed as dist
+
+    from mlbricks_b200.elasticbit import tensor_parallel as tp
+
+    coll = tp.Collectives.from_group() if world > 1 else None
+    layers, head, bits_of = build_stack(device, world, rank, coll)
+    out = {"workload": "config5: 32 x (QKV 4096->6144 col, O 4096->4096 row, gate/up 4096->14336 "
+                       "col, down 14336->4096 row) + lm_head 4096->128256 col, threshold 0.01; "
+                       f"Megatron TP over {world} GPU(s), NCCL all-reduce of fp32 partials; "
+                       "one CUDA graph per decode step",
+           "bits": bits_of, "decode_tok_s": {}}
+    stream = torch.cuda.Stream(device)
+    for M in (1, 16, 64):
+        h0 = torch.randn((M, 4096), device=device, dtype=torch.float16)
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                logits = stack_step(layers, head, h0, world)
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            logits = stack_step(layers, head, h0, world)
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                g.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        steps = max(3, min(args.steps, 20))
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):  # replay runs on the current stream
+            a.record(stream)
+            for _ in range(steps):
+                g.replay()
+            b.record(stream)
+        b.synchronize()
+        t = torch.tensor([a.elapsed_time(b)], device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        out["decode_tok_s"][str(M)] = round(M * steps / (float(t.item()) * 1e-3), 1)
+        del g, logits
+    # 2048-token prefill (tensor-core GEMM route)
+    x = torch.randn((2048, 4096), device=device, dtype=torch.float16)
+    with torch.cuda.stream(stream):
+        stack_step(layers, head, x, world)
+        stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        stack_step(layers, head, x, world)
+        b.record(stream)
+    b.synchronize()
+    t = torch.tensor([a.elapsed_time(b)], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    out["prefill2048_tok_s"] = round(2048 / (float(t.item()) * 1e-3), 1)
+    del layers, head
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_prefill(mats, device, lib, args) -> dict:
@@ -458,7 +605,7 @@ def run_reference(args) -> None:
         return
     secs = max(2.0, min(20.0, 2.0 * (args.steps + args.warmup)))
     cb = cpu_baseline(seconds=secs)
-    print(json.dumps({
+    emit({
         "impl": "reference",
         "metric": METRIC, "value": cb["value"], "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
@@ -470,7 +617,7 @@ def run_reference(args) -> None:
         "cpu_baseline": cb,
         "e2e": {"value": cb["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-    }))
+    })
 
 
 def run_single(args) -> None:
@@ -548,10 +695,28 @@ def run_single(args) -> None:
             mus = a.elapsed_time(b) * 1e3 / (reps * len(mats))
             out.update({"materialize_us": round(mus, 3),
                         "gemm_TFLOPs": round(2.0 * M * N * K / ((us - mus) * 1e-6) / 1e12, 1)})
-    print(json.dumps(out))
+    emit(out)
+
+
+_JSON_FD = None
+
+
+def emit(obj) -> None:
+    """Write one JSON line to the real stdout; library chatter (NCCL banners) is sent
+    to stderr by main() so stdout carries nothing but the result line."""
+    line = (json.dumps(obj) + "\n").encode()
+    if _JSON_FD is None:
+        sys.stdout.write(line.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_JSON_FD, line)
 
 
 def main() -> None:
+    global _JSON_FD
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--single", default=None, help="K,N,M: one launch shape (profiling)")
     ap.add_argument("--copies", type=int, default=3)
@@ -564,6 +729,7 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-tp-stack", action="store_true")
     args = ap.parse_args()
     if args.single:
         run_single(args)

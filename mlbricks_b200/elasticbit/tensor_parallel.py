@@ -1,0 +1,165 @@
+"""Megatron-style tensor parallelism for compressed ElasticBit linears.
+
+The reference has no distributed code; this module adds the multi-GPU form of
+the same forward.  A matrix is compressed once, globally (bits, codes and row
+scales are exactly the single-GPU ones), then sliced:
+
+* ``column`` parallel (QKV, gate/up, lm_head): rank r keeps output rows
+  [r*N/W, (r+1)*N/W) and their scales; no collective -- the output stays
+  sharded along features (``gather=True`` all-gathers it);
+* ``row`` parallel (O, down): rank r keeps input columns [r*K/W, (r+1)*K/W)
+  and all row scales; each rank produces the fp32 partial sum over its K slice
+  (libebx ``y32``), one all-reduce (sum, fp32) combines them, and the bias is
+  added before the single fp16 rounding -- the same arithmetic as the unsharded
+  kernel up to fp32 summation order.
+
+Everything here is host orchestration; the per-rank compute is libebx
+(``RuntimeMatrix.linear``).  The collective is pluggable (``allreduce`` /
+``allgather`` callables) so the orchestration can be exercised with gloo ranks on
+CPU and a stand-in compute function.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+import numpy as np
+import torch
+
+MODES = ("column", "row")
+
+
+def shard_bounds(total: int, world: int, rank: int, align: int = 1) -> tuple[int, int]:
+    """[lo, hi) of rank's slice; every interior boundary is a multiple of `align`."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("invalid rank/world")
+    units = -(-total // align)
+    lo = (units * rank) // world * align
+    hi = (units * (rank + 1)) // world * align
+    return min(lo, total), min(hi, total)
+
+
+def shard_codes(codes, scales, mode: str, world: int, rank: int):
+    """Slice globally selected int16 codes [N, K] and fp32 scales [N] for one rank.
+
+    Column shards are aligned to 16 rows (one row group), row shards to 64
+    columns (one k-tile) so every shard keeps the device tile layout dense.
+    Works on numpy arrays or torch tensors.
+    """
+    if mode not in MODES:
+        raise ValueError(f"mode must be one of {MODES}")
+    N, K = int(codes.shape[0]), int(codes.shape[1])
+    if mode == "column":
+        lo, hi = shard_bounds(N, world, rank, align=16)
+        return codes[lo:hi], scales[lo:hi], (lo, hi)
+    lo, hi = shard_bounds(K, world, rank, align=64)
+    return codes[:, lo:hi], scales, (lo, hi)
+
+
+@dataclass
+class Collectives:
+    """The two collectives a sharded linear needs (defaults: torch.distributed)."""
+    allreduce: Callable[[torch.Tensor], None]
+    allgather: Callable[[torch.Tensor], torch.Tensor]
+
+    @staticmethod
+    def from_group(group=None) -> "Collectives":
+        import torch.distributed as dist
+
+        def allreduce(t: torch.Tensor) -> None:
+            dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
+
+        def allgather(t: torch.Tensor) -> torch.Tensor:
+            world = dist.get_world_size(group)
+            parts = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(parts, t.contiguous(), group=group)
+            return torch.cat(parts, dim=-1)
+
+        return Collectives(allreduce, allgather)
+
+
+class ShardedLinear(torch.nn.Module):
+    """One rank's part of a tensor-parallel compressed linear.
+
+    ``local`` computes y_local = x @ W_shard^T for the shard; by default it is
+    the shard RuntimeMatrix's libebx call (fp32 partial for row mode).
+    """
+
+    def __init__(self, matrix, mode: str, out_features: int, in_features: int,
+                 bounds: tuple[int, int], bias: torch.Tensor | None = None,
+                 collectives: Collectives | None = None,
+                 local: Callable[[torch.Tensor, bool], torch.Tensor] | None = None,
+                 gather: bool = False, input_is_local: bool = False) -> None:
+        super().__init__()
+        if mode not in MODES:
+            raise ValueError(f"mode must be one of {MODES}")
+        self.matrix = matrix
+        self.mode = mode
+        self.out_features = int(out_features)
+        self.in_features = int(in_features)
+        self.bounds = bounds
+        self.gather = bool(gather)
+        self.input_is_local = bool(input_is_local)  # row mode: x already holds this K slice
+        self.collectives = collectives
+        self._local = local
+        if bias is None:
+            self.register_parameter("bias", None)
+        else:
+            b = bias.detach()
+            if mode == "column":
+                b = b[bounds[0]:bounds[1]]
+            self.bias = torch.nn.Parameter(b.clone(), requires_grad=False)
+
+    def _compute(self, x: torch.Tensor, fp32: bool, bias: torch.Tensor | None) -> torch.Tensor:
+        if self._local is not None:
+            y = self._local(x, fp32)
+            if bias is not None:  # stand-in compute: bias before the single rounding
+                y = (y.float() + bias.float()).to(y.dtype)
+            return y
+        native = getattr(self.matrix, "_native", self.matrix)
+        if fp32:
+            return native.linear(x, None, out32=True)[1]
+        return native.linear(x, bias)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.mode == "column":
+            if x.shape[-1] != self.in_features:
+                raise ValueError(f"expected last dimension {self.in_features}")
+            y = self._compute(x, False, self.bias)
+            if self.gather:
+                if self.collectives is None:
+                    raise RuntimeError("column gather needs collectives")
+                y = self.collectives.allgather(y)
+            return y
+        # row parallel: x is the full activation; use this rank's K slice
+        lo, hi = self.bounds
+        xs = x.contiguous() if self.input_is_local else x[..., lo:hi].contiguous()
+        part = self._compute(xs, True, None)
+        if self.collectives is not None:
+            self.collectives.allreduce(part)
+        if self.bias is not None:
+            part = part + self.bias.float()
+        return part.to(torch.float16)
+
+
+def build_sharded(codes, scales, bits: int, mode: str, world: int, rank: int, *,
+                  threshold: float = 0.0, error: float = 0.0, bias=None,
+                  collectives: Collectives | None = None, gather: bool = False,
+                  input_is_local: bool = False,
+                  decodePolicy: str = "fullPrecision") -> ShardedLinear:
+    """Create this rank's shard (libebx matrix) from the global analyzer result."""
+    from .core import RuntimeMatrix
+
+    N, K = int(codes.shape[0]), int(codes.shape[1])
+    c, s, bounds = shard_codes(codes, scales, mode, world, rank)
+    if torch.is_tensor(c):
+        c = c.contiguous()
+    else:
+        c = np.ascontiguousarray(c)
+    m = RuntimeMatrix._compressSelectedCodes(c, s, bits, threshold, error,
+                                             decodePolicy=decodePolicy)
+    return ShardedLinear(m, mode, N, K, bounds, bias=bias, collectives=collectives, gather=gather,
+                         input_is_local=input_is_local)
+
+
+__all__ = ["MODES", "shard_bounds", "shard_codes", "Collectives", "ShardedLinear", "build_sharded"]
