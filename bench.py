@@ -346,7 +346,7 @@ def quantize_rows(w16, bits: int):
     return q, sc
 
 
-def build_stack(device, world: int, rank: int, collectives):
+def build_stack(device, world: int, rank: int, collectives, exchange=None):
     """Compress the stack once per shape-class with the analyzer (threshold 0.01,
     32 calibration rows), then quantise every layer's seeded weight at that width
     and keep this rank's Megatron shard."""
@@ -363,16 +363,24 @@ def build_stack(device, world: int, rank: int, collectives):
         b, _, _, _ = _selectBitsTorch(w, calib, 0.01)
         bits_of[name] = min(b, 15)
         del w
+    fuse_gate_up = bits_of["gate"] == bits_of["up"]
     layers = []
     for li in range(STACK_LAYERS):
-        layer = {}
+        layer, pending = {}, {}
         for mi, (name, K, N, mode) in enumerate(STACK_MATS):
             w = baseline_weights_gpu(N, K, 10_000 + li * 16 + mi, device)
             q, sc = quantize_rows(w, bits_of[name])
             del w
+            if fuse_gate_up and name in ("gate", "up"):
+                pending[name] = (q, sc)
+                if len(pending) == 2:  # one launch for both: [gate rows | up rows] of this rank
+                    layer["gate_up"] = tp.build_column_fused([pending["gate"], pending["up"]],
+                                                             bits_of["gate"], world, rank)
+                    pending.clear()
+                continue
             layer[name] = tp.build_sharded(q, sc, bits_of[name], mode, world, rank,
                                            collectives=collectives,
-                                           input_is_local=(mode == "row"))
+                                           input_is_local=(mode == "row"), exchange=exchange)
             del q, sc
         layers.append(layer)
     name, K, N, mode = STACK_HEAD
@@ -394,9 +402,12 @@ def stack_step(layers, head, h, world: int):
         qkv = L["qkv"](h)                               # [M, 6144 / W] local
         attn = qkv[:, : 4096 // world]                  # local heads -> O's K slice
         h = L["o"](attn)                                # all-reduce -> [M, 4096]
-        g = L["gate"](h)
-        u = L["up"](h)
-        act = (torch.nn.functional.silu(g.float()) * u.float()).to(torch.float16)
+        if "gate_up" in L:
+            gu = L["gate_up"](h)                        # [M, 2 * 14336 / W] local
+            g, u = gu.split(L["gate_up"].part_widths, dim=-1)
+        else:
+            g, u = L["gate"](h), L["up"](h)
+        act = torch.nn.functional.silu(g) * u           # fp16
         h = L["down"](act)                              # all-reduce -> [M, 4096]
     return head(h)
 
@@ -408,11 +419,17 @@ def run_tp_stack(args, world: int, rank: int, device) -> dict:
     from mlbricks_b200.elasticbit import tensor_parallel as tp
 
     coll = tp.Collectives.from_group() if world > 1 else None
-    layers, head, bits_of = build_stack(device, world, rank, coll)
+    # decode batches <= 16: row-parallel layers all-reduce through the libebx exchange
+    # (fp32 partials stored into every rank's region over NVLink); larger M: NCCL
+    exchange = (tp.Exchange.from_group(16, 4096)
+                if world > 1 and not getattr(args, "nccl_only", False) else None)
+    layers, head, bits_of = build_stack(device, world, rank, coll, exchange)
     out = {"workload": "config5: 32 x (QKV 4096->6144 col, O 4096->4096 row, gate/up 4096->14336 "
                        "col, down 14336->4096 row) + lm_head 4096->128256 col, threshold 0.01; "
-                       f"Megatron TP over {world} GPU(s), NCCL all-reduce of fp32 partials; "
-                       "one CUDA graph per decode step",
+                       f"Megatron TP over {world} GPU(s); row-parallel all-reduce: "
+                       + ("libebx exchange (M<=16), NCCL fp32 (M>16)" if exchange else
+                          "NCCL fp32" if world > 1 else "none") +
+                       "; gate/up fused per rank; one CUDA graph per decode step",
            "bits": bits_of, "decode_tok_s": {}}
     stream = torch.cuda.Stream(device)
     for M in (1, 16, 64):
@@ -462,6 +479,10 @@ def run_tp_stack(args, world: int, rank: int, device) -> dict:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     out["prefill2048_tok_s"] = round(2048 / (float(t.item()) * 1e-3), 1)
     del layers, head
+    if exchange is not None:
+        torch.cuda.synchronize()
+        dist.barrier()  # no rank still writes into a region that is about to be freed
+        exchange.close()
     torch.cuda.empty_cache()
     return out
 
@@ -730,6 +751,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-tp-stack", action="store_true")
+    ap.add_argument("--nccl-only", action="store_true",
+                    help="tp stack: all-reduce through NCCL even for M <= 16")
     args = ap.parse_args()
     if args.single:
         run_single(args)

@@ -166,9 +166,10 @@ EBX_API ebx_status ebx_quantize(const float* weights, int32_t rows, int32_t cols
 EBX_API ebx_status ebx_weights_to_fp16(const float* weights, int64_t n, void* out, void* stream);
 
 /* Device health word of `device`: 0 = healthy, nonzero = a kernel's bounded
- * wait on a TMA copy gave up (the kernel then returned early; its outputs are
- * unspecified).  `clear` = 1 resets it.  Synchronizes the device's legacy
- * stream.  No reference counterpart: the reference kernels never wait. */
+ * wait (on a TMA copy, or on a peer's exchange flag) gave up (the kernel then
+ * returned early; its outputs are unspecified).  `clear` = 1 resets it.
+ * Synchronizes the device's legacy stream.  No reference counterpart: the
+ * reference kernels never wait. */
 EBX_API ebx_status ebx_device_status(int32_t device, int32_t* status, int32_t clear);
 
 /* FNV-1a 64 of a HOST byte range: the MLB4 scale/payload checksum
@@ -186,6 +187,50 @@ EBX_API ebx_status ebx_elastic_linear_packed(const void* x, int32_t x_dtype, int
                                      int32_t scale_dtype, const void* bias, int32_t bits,
                                      int64_t group_size, int64_t out_features,
                                      int64_t in_features, void* out, void* stream);
+
+/* ---- Tensor-parallel exchange (row-parallel linear + all-reduce) ----------
+ * No reference counterpart: the reference has no distributed code.  These
+ * replace "row-parallel shard GEMV, then an NCCL all-reduce of the fp32
+ * partials, then bias and one fp16 rounding" for decode-sized M (<= 16) with
+ * a one-shot exchange over NVLink peer memory, one process per GPU:
+ *
+ *   1. every rank: ebx_exchange_create -> a device region (flags + two slots
+ *      of world * max_m * max_n fp32 partials) and an opaque handle blob of
+ *      EBX_EXCHANGE_HANDLE_BYTES (CUDA IPC handle, GPU UUID, shape);
+ *   2. the caller all-gathers the blobs (any host transport) and passes all
+ *      of them, in rank order, to ebx_exchange_connect, which maps every
+ *      peer's region (cudaIpcOpenMemHandle);
+ *   3. ebx_linear_allreduce: the shard's decode kernel stores its fp32
+ *      partial sums straight into every rank's region and, once all of its
+ *      CTAs are done, publishes an epoch flag to every rank (release, system
+ *      scope); a finish kernel waits (bounded, ~2 s) for the flags of all
+ *      ranks, sums the partials in rank order 0..world-1, adds bias in fp32
+ *      and rounds once to fp16.  Every rank gets bit-identical outputs.
+ *
+ * All ranks must issue the same sequence of ebx_linear_allreduce calls with
+ * the same M and shard shape; the epoch lives in device memory, so the calls
+ * may be captured in a CUDA graph.  Ranks must be on distinct GPUs (connect
+ * refuses otherwise).  A wait that gives up sets the device status word
+ * (ebx_device_status) and leaves y unwritten; the exchange is then out of
+ * step and must be destroyed. */
+#define EBX_EXCHANGE_HANDLE_BYTES 128
+
+typedef struct ebx_exchange ebx_exchange;
+
+/* Allocate this rank's region on `device`; 1 <= world <= 8, 1 <= max_m <= 16.
+ * handle_out receives EBX_EXCHANGE_HANDLE_BYTES bytes. */
+EBX_API ebx_status ebx_exchange_create(int32_t world, int32_t rank, int32_t device, int64_t max_m,
+                                       int64_t max_n, void* handle_out, ebx_exchange** out);
+/* Map the regions of all ranks: `handles` = world blobs in rank order. */
+EBX_API ebx_status ebx_exchange_connect(ebx_exchange* ex, const void* handles);
+EBX_API ebx_status ebx_exchange_destroy(ebx_exchange* ex);
+/* y[M, rows] (fp16, DEVICE) = fp16( sum over ranks of x_r @ W_r^T + bias ), where
+ * this rank holds W_r (its K slice of the weight, all rows) and x_r [M, cols]
+ * (its slice of the activations).  bias (fp16, may be NULL) and y32 (fp32
+ * copy before rounding, may be NULL) as in ebx_linear. */
+EBX_API ebx_status ebx_linear_allreduce(const ebx_matrix* m, const void* x, int64_t M,
+                                        const void* bias, void* y, float* y32, ebx_exchange* ex,
+                                        void* stream);
 
 #ifdef __cplusplus
 }

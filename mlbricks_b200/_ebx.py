@@ -28,6 +28,8 @@ EBX_ERR_UNSUPPORTED = 3
 EBX_ERR_WORKSPACE = 4
 EBX_ERR_CODE_RANGE = 5
 
+EXCHANGE_HANDLE_BYTES = 128  # EBX_EXCHANGE_HANDLE_BYTES
+
 # Every symbol include/ebx.h declares, with (restype, argtypes).
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
@@ -71,6 +73,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ebx_weights_to_fp16": (_ST, [_P, _I64, _P, _P]),
     "ebx_device_status": (_ST, [_I32, ctypes.POINTER(_I32), _I32]),
     "ebx_fnv1a64": (_U64, [_P, _U64]),
+    "ebx_exchange_create": (_ST, [_I32, _I32, _I32, _I64, _I64, _P, ctypes.POINTER(_P)]),
+    "ebx_exchange_connect": (_ST, [_P, _P]),
+    "ebx_exchange_destroy": (_ST, [_P]),
+    "ebx_linear_allreduce": (_ST, [_P, _P, _I64, _P, _P, _P, _P, _P]),
     "ebx_elastic_linear_packed": (
         _ST, [_P, _I32, _I64, _P, _P, _I32, _P, _I32, _I64, _I64, _I64, _P, _P]),
 }

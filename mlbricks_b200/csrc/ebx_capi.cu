@@ -21,6 +21,28 @@ struct ebx_matrix {
     ebx::Matrix m;
 };
 
+// Handle blob exchanged between ranks (EBX_EXCHANGE_HANDLE_BYTES).
+struct ExchangeBlob {
+    cudaIpcMemHandle_t ipc;   // 64 bytes: this rank's region
+    unsigned char uuid[16];   // GPU identity: ranks must be on distinct GPUs
+    int32_t world, rank;
+    int64_t max_m, max_n;
+    uint64_t bytes;
+    unsigned char pad[EBX_EXCHANGE_HANDLE_BYTES - 64 - 16 - 8 - 24];
+};
+static_assert(sizeof(ExchangeBlob) == EBX_EXCHANGE_HANDLE_BYTES, "exchange blob size");
+
+struct ebx_exchange {
+    ebx::XchgArgs xa;          // peer pointers (valid after connect)
+    int device = 0;
+    int64_t max_m = 0, max_n = 0;
+    uint8_t* own = nullptr;    // cudaMalloc'd region of this rank
+    uint64_t bytes = 0;
+    bool connected = false;
+    bool mapped[ebx::kMaxWorld] = {};
+    ExchangeBlob blob;
+};
+
 namespace ebx {
 
 static thread_local std::string g_last_error;
@@ -373,10 +395,168 @@ ebx_status ebx_device_status(int32_t device, int32_t* status, int32_t clear) {
     }
     DeviceGuard g(device);
     if (!g.ok) return cuda_fail(cudaErrorInvalidDevice, "cudaSetDevice");
-    int v = 0, vg = 0;
+    int v = 0, vg = 0, vx = 0;
     EBX_CUDA(ebx::read_device_status(&v, clear != 0, nullptr));
     EBX_CUDA(ebx::read_gemm_status(&vg, clear != 0, nullptr));
-    *status = v ? v : vg;
+    EBX_CUDA(ebx::read_xchg_status(&vx, clear != 0, nullptr));
+    *status = v ? v : (vg ? vg : vx);
+    return EBX_OK;
+}
+
+// ---- tensor-parallel exchange ----------------------------------------------
+
+ebx_status ebx_exchange_create(int32_t world, int32_t rank, int32_t device, int64_t max_m,
+                               int64_t max_n, void* handle_out, ebx_exchange** out) {
+    if (!handle_out || !out) {
+        set_error("null argument");
+        return EBX_ERR_INVALID;
+    }
+    *out = nullptr;
+    if (world < 1 || world > ebx::kMaxWorld || rank < 0 || rank >= world) {
+        set_error("exchange: need 1 <= world <= 8 and 0 <= rank < world");
+        return EBX_ERR_INVALID;
+    }
+    if (max_m < 1 || max_m > 16 || max_n < 1 || max_n > (int64_t(1) << 24)) {
+        set_error("exchange: need 1 <= max_m <= 16 and 1 <= max_n <= 2^24");
+        return EBX_ERR_INVALID;
+    }
+    DeviceGuard g(device);
+    if (!g.ok) return cuda_fail(cudaErrorInvalidDevice, "cudaSetDevice");
+    cudaDeviceProp prop;
+    EBX_CUDA(cudaGetDeviceProperties(&prop, device));
+    ebx_exchange* ex = new (std::nothrow) ebx_exchange();
+    if (!ex) {
+        set_error("out of host memory");
+        return EBX_ERR_INVALID;
+    }
+    ex->device = device;
+    ex->max_m = max_m;
+    ex->max_n = max_n;
+    ex->xa.world = world;
+    ex->xa.rank = rank;
+    ex->bytes = ebx::kXchgDataOff + 2ull * uint64_t(world) * uint64_t(max_m) * uint64_t(max_n) * 8ull;
+    cudaError_t e = cudaMalloc(&ex->own, ex->bytes);
+    if (e == cudaSuccess) e = cudaMemset(ex->own, 0, ex->bytes);
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&ex->blob.ipc, ex->own);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        if (ex->own) cudaFree(ex->own);
+        delete ex;
+        return cuda_fail(e, "ebx_exchange_create");
+    }
+    std::memcpy(ex->blob.uuid, &prop.uuid, 16);
+    ex->blob.world = world;
+    ex->blob.rank = rank;
+    ex->blob.max_m = max_m;
+    ex->blob.max_n = max_n;
+    ex->blob.bytes = ex->bytes;
+    std::memset(ex->blob.pad, 0, sizeof(ex->blob.pad));
+    std::memcpy(handle_out, &ex->blob, sizeof(ExchangeBlob));
+    *out = ex;
+    return EBX_OK;
+}
+
+ebx_status ebx_exchange_connect(ebx_exchange* ex, const void* handles) {
+    if (!ex || !handles) {
+        set_error("null argument");
+        return EBX_ERR_INVALID;
+    }
+    if (ex->connected) {
+        set_error("exchange already connected");
+        return EBX_ERR_INVALID;
+    }
+    const int world = ex->xa.world, rank = ex->xa.rank;
+    std::vector<ExchangeBlob> b(world);
+    std::memcpy(b.data(), handles, sizeof(ExchangeBlob) * size_t(world));
+    for (int r = 0; r < world; ++r) {
+        if (b[r].world != world || b[r].rank != r || b[r].max_m != ex->max_m ||
+            b[r].max_n != ex->max_n || b[r].bytes != ex->bytes) {
+            set_error("exchange: handle " + std::to_string(r) +
+                      " does not match (world, rank order, max_m, max_n)");
+            return EBX_ERR_INVALID;
+        }
+        for (int q = 0; q < r; ++q)
+            if (std::memcmp(b[q].uuid, b[r].uuid, 16) == 0) {
+                set_error("exchange: ranks " + std::to_string(q) + " and " + std::to_string(r) +
+                          " share one GPU; the exchange needs one GPU per rank");
+                return EBX_ERR_UNSUPPORTED;
+            }
+    }
+    if (std::memcmp(&b[rank], &ex->blob, sizeof(ExchangeBlob)) != 0) {
+        set_error("exchange: handle of this rank is not the one ebx_exchange_create returned");
+        return EBX_ERR_INVALID;
+    }
+    DeviceGuard g(ex->device);
+    if (!g.ok) return cuda_fail(cudaErrorInvalidDevice, "cudaSetDevice");
+    for (int r = 0; r < world; ++r) {
+        if (r == rank) {
+            ex->xa.peer[r] = ex->own;
+            continue;
+        }
+        void* p = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&p, b[r].ipc, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (int q = 0; q < r; ++q)
+                if (ex->mapped[q]) {
+                    cudaIpcCloseMemHandle(ex->xa.peer[q]);
+                    ex->mapped[q] = false;
+                }
+            return cuda_fail(e, "cudaIpcOpenMemHandle");
+        }
+        ex->xa.peer[r] = static_cast<uint8_t*>(p);
+        ex->mapped[r] = true;
+    }
+    ex->connected = true;
+    return EBX_OK;
+}
+
+ebx_status ebx_exchange_destroy(ebx_exchange* ex) {
+    if (!ex) return EBX_OK;
+    DeviceGuard g(ex->device);
+    cudaError_t first = cudaSuccess;
+    for (int r = 0; r < ebx::kMaxWorld; ++r)
+        if (ex->mapped[r]) {
+            const cudaError_t e = cudaIpcCloseMemHandle(ex->xa.peer[r]);
+            if (first == cudaSuccess) first = e;
+        }
+    if (ex->own) {
+        const cudaError_t e = cudaFree(ex->own);
+        if (first == cudaSuccess) first = e;
+    }
+    delete ex;
+    if (first != cudaSuccess) return cuda_fail(first, "ebx_exchange_destroy");
+    return EBX_OK;
+}
+
+ebx_status ebx_linear_allreduce(const ebx_matrix* h, const void* x, int64_t M, const void* bias,
+                                void* y, float* y32, ebx_exchange* ex, void* stream) {
+    if (!h || !ex || (M > 0 && (!x || !y))) {
+        set_error("null argument");
+        return EBX_ERR_INVALID;
+    }
+    if (!ex->connected) {
+        set_error("exchange not connected (ebx_exchange_connect)");
+        return EBX_ERR_INVALID;
+    }
+    if (M < 0 || M > ex->max_m || int64_t(h->m.rows) > ex->max_n) {
+        set_error("ebx_linear_allreduce: need 0 <= M <= max_m and rows <= max_n of the exchange");
+        return EBX_ERR_INVALID;
+    }
+    if (h->m.device != ex->device) {
+        set_error("matrix and exchange live on different devices");
+        return EBX_ERR_INVALID;
+    }
+    if (M == 0) return EBX_OK;
+    DeviceGuard g(h->m.device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    ebx::XchgArgs xa = ex->xa;
+    // fused: the decode kernel reduces and writes y itself; else the finish kernel does
+    EBX_CUDA(ebx::launch_decode(h->m, static_cast<const uint16_t*>(x), M,
+                                static_cast<const uint16_t*>(bias), static_cast<uint16_t*>(y), y32,
+                                s, &xa));
+    if (!xa.fused)
+        EBX_CUDA(ebx::launch_xchg_finish(xa, int(M), h->m.rows, static_cast<const uint16_t*>(bias),
+                                         static_cast<uint16_t*>(y), y32, s));
     return EBX_OK;
 }
 

@@ -26,12 +26,18 @@
 
 #include "ebx_common.cuh"
 #include "ebx_internal.h"
+#include "ebx_xchg.cuh"
 
 namespace ebx {
 namespace {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
+
+// Device health word: bounded waits that give up record their code here.
+__device__ int g_device_status = 0;
+constexpr int kDeviceTimeout = 0x7101;
+constexpr uint32_t kWaitLimit = 1u << 24;
 
 struct DecodeArgs {
     const uint8_t* tiles;
@@ -46,7 +52,20 @@ struct DecodeArgs {
     uint32_t magic;   // 0x4B000000 (2^23), passed in so the compiler keeps it in a register
     int stages;       // pipe kernel: ring depth (runtime, <= kMaxStages)
     int stage_bytes;  // pipe kernel: RG weight rounds + (min(M, 8 NT) + 1) activation rows
+    XchgArgs xa;      // world > 0: fp32 partials go to the tensor-parallel exchange
 };
+
+// Fused exchange: all ranks' partials of (tok, row) -> bias -> one fp16 rounding.
+__device__ __forceinline__ void xchg_finish_one(const DecodeArgs& a, uint32_t e, int tok, int row) {
+    float v;
+    if (!xchg_gather(a.xa, e, a.M, a.N, tok, row, v)) {
+        atomicExch(&g_device_status, kXchgTimeout);
+        return;
+    }
+    if (a.bias) v += __half2float(__ushort_as_half(a.bias[row]));
+    a.y[size_t(tok) * a.N + row] = __half_as_ushort(__float2half_rn(v));
+    if (a.y32) a.y32[size_t(tok) * a.N + row] = v;
+}
 
 template <int B, int NT, bool VECX>
 struct StageLayout {
@@ -71,6 +90,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
     const int c = lane & 3;
     const int row_lo = g * kRowGroup + r0;
     const int row_hi = row_lo + 8;
+    const uint32_t xe = a.xa.world ? xchg_epoch(a.xa) + 1u : 0u;  // epoch this call publishes
 
     uint64_t nb2 = 0, slo2 = 0, shi2 = 0;
     if constexpr (B != kFp16Bits) {
@@ -211,10 +231,23 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         const int tok = 8 * nb + (l & 3) * 2 + (i & 1);
         if (row < a.N && tok < a.M) {
             if constexpr (HW && B != kFp16Bits) v = v * a.scales[row];
-            if (a.bias) v += __half2float(__ushort_as_half(a.bias[row]));
-            a.y[size_t(tok) * a.N + row] = __half_as_ushort(__float2half_rn(v));
-            if (a.y32) a.y32[size_t(tok) * a.N + row] = v;
+            if (a.xa.world) {
+                xchg_push(a.xa, xe, a.M, a.N, tok, row, v);
+            } else {
+                if (a.bias) v += __half2float(__ushort_as_half(a.bias[row]));
+                a.y[size_t(tok) * a.N + row] = __half_as_ushort(__float2half_rn(v));
+                if (a.y32) a.y32[size_t(tok) * a.N + row] = v;
+            }
         }
+    }
+    if (a.xa.world && a.xa.fused) {
+        for (int idx = threadIdx.x; idx < NT * 128; idx += kThreads) {
+            const int l = (idx >> 2) & 31, i = idx & 3;
+            const int row = g * kRowGroup + (l >> 2) + 8 * (i >> 1);
+            const int tok = 8 * (idx >> 7) + (l & 3) * 2 + (i & 1);
+            if (row < a.N && tok < a.M) xchg_finish_one(a, xe, tok, row);
+        }
+        xchg_advance(a.xa, xe);
     }
 }
 
@@ -228,9 +261,6 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
 // ahead.  Every mbarrier wait is bounded: after kWaitLimit probes the warp
 // records EBX_DEVICE_TIMEOUT in g_device_status, drains its own copies (again
 // bounded) and leaves the loop, so a stuck copy cannot hang the GPU.
-__device__ int g_device_status = 0;
-constexpr int kDeviceTimeout = 0x7101;
-constexpr uint32_t kWaitLimit = 1u << 24;
 
 __device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity) {
     for (uint32_t it = 0; it < kWaitLimit; ++it)
@@ -279,6 +309,7 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
     const int lane = threadIdx.x & 31;
     const int rounds = (a.kt + kWarps - 1) / kWarps;
     const int mrows = a.M < NT * 8 ? a.M : NT * 8;
+    const uint32_t xe = a.xa.world ? xchg_epoch(a.xa) + 1u : 0u;  // epoch this call publishes
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < D; ++i) {
@@ -464,17 +495,66 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
         const int tok = 8 * nb + (l & 3) * 2 + (i & 1);
         if (g < a.groups && row < a.N && tok < a.M) {
             if constexpr (HW && B != kFp16Bits) v = v * a.scales[row];
-            if (a.bias) v += __half2float(__ushort_as_half(a.bias[row]));
-            a.y[size_t(tok) * a.N + row] = __half_as_ushort(__float2half_rn(v));
-            if (a.y32) a.y32[size_t(tok) * a.N + row] = v;
+            if (a.xa.world) {
+                xchg_push(a.xa, xe, a.M, a.N, tok, row, v);
+            } else {
+                if (a.bias) v += __half2float(__ushort_as_half(a.bias[row]));
+                a.y[size_t(tok) * a.N + row] = __half_as_ushort(__float2half_rn(v));
+                if (a.y32) a.y32[size_t(tok) * a.N + row] = v;
+            }
         }
+    }
+    if (a.xa.world && a.xa.fused) {
+        // every CTA of the grid is resident (cooperative launch) and has pushed
+        // before it waits, so each rank's CTAs eventually deliver
+        for (int idx = threadIdx.x; idx < RG * NT * 128; idx += blockDim.x) {
+            const int rgl = idx / (NT * 128);
+            const int rem = idx % (NT * 128);
+            const int nb = rem >> 7, l = (rem >> 2) & 31, i = rem & 3;
+            const int g = blockIdx.x * RG + rgl;
+            const int row = g * kRowGroup + (l >> 2) + 8 * (i >> 1);
+            const int tok = 8 * nb + (l & 3) * 2 + (i & 1);
+            if (g < a.groups && row < a.N && tok < a.M) xchg_finish_one(a, xe, tok, row);
+        }
+        xchg_advance(a.xa, xe);
     }
 }
 
 constexpr int kStages = 4;
 
+// Exchange launches: fused (reduce inside the decode kernel) only when the whole
+// grid fits on the GPU at once; the launch is then cooperative, which makes the
+// runtime guarantee that co-residency, so CTAs that wait for peers' partials can
+// never hold back CTAs of their own grid that those peers wait for in turn.
+template <typename Kern>
+cudaError_t launch_maybe_xchg(Kern kern, DecodeArgs& a, unsigned grid, unsigned threads, int smem,
+                              cudaStream_t s) {
+    if (!a.xa.world) {
+        kern<<<grid, threads, smem, s>>>(a);
+        return cudaGetLastError();
+    }
+    int dev = 0, sms = 0, per_sm = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess)
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, int(threads), size_t(smem));
+    if (e != cudaSuccess) return e;
+    a.xa.fused = int64_t(grid) <= int64_t(per_sm) * sms ? 1 : 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = size_t(smem);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = a.xa.fused ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
 template <int B, bool HW, int NT, bool VECX>
-cudaError_t launch_one(const DecodeArgs& a, int groups, cudaStream_t s) {
+cudaError_t launch_one(DecodeArgs& a, int groups, cudaStream_t s) {
     using L = StageLayout<B, NT, VECX>;
     constexpr int ring = kWarps * kStages * L::kStage;
     constexpr int red = kWarps * NT * 128 * 4;
@@ -491,12 +571,11 @@ cudaError_t launch_one(const DecodeArgs& a, int groups, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         configured.fetch_or(bit);
     }
-    kern<<<groups, kThreads, smem, s>>>(a);
-    return cudaGetLastError();
+    return launch_maybe_xchg(kern, a, unsigned(groups), kThreads, smem, s);
 }
 
 template <int B, bool HW, int NT, bool DIRECT, int RG>
-cudaError_t launch_pipe(DecodeArgs a, int groups, cudaStream_t s) {
+cudaError_t launch_pipe(DecodeArgs& a, int groups, cudaStream_t s) {
     using S = PipeStage<B, NT, RG>;
     // RG == 1: three CTAs per SM (27 warps); RG == 2: one CTA per SM.  The ring
     // is as deep as that budget allows for this M (2..kMaxStages stages).
@@ -520,12 +599,11 @@ cudaError_t launch_pipe(DecodeArgs a, int groups, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         configured.fetch_or(bit);
     }
-    kern<<<(groups + RG - 1) / RG, kThreads * RG + 32, smem, s>>>(a);
-    return cudaGetLastError();
+    return launch_maybe_xchg(kern, a, unsigned((groups + RG - 1) / RG), kThreads * RG + 32, smem, s);
 }
 
 template <int B, bool HW>
-cudaError_t dispatch_nt(const DecodeArgs& a, int groups, bool pipe, bool direct, cudaStream_t s) {
+cudaError_t dispatch_nt(DecodeArgs& a, int groups, bool pipe, bool direct, cudaStream_t s) {
     if (pipe) {
         constexpr bool kCanDirect = !HW && B != kFp16Bits;
         if (a.M <= 8) {
@@ -555,8 +633,9 @@ cudaError_t read_device_status(int* status, bool clear, cudaStream_t s) {
 }
 
 cudaError_t launch_decode(const Matrix& m, const uint16_t* x, int64_t M, const uint16_t* bias,
-                          uint16_t* y, float* y32, cudaStream_t s) {
+                          uint16_t* y, float* y32, cudaStream_t s, XchgArgs* xa) {
     if (M <= 0) return cudaSuccess;
+    if (xa && M > 16) return cudaErrorInvalidValue;  // one launch = one exchange epoch
     const bool vecx = (m.cols % 64) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
     const bool hw = m.exec_width < 16 && m.bits <= 8;
     for (int64_t m0 = 0; m0 < M; m0 += 16) {
@@ -565,8 +644,9 @@ cudaError_t launch_decode(const Matrix& m, const uint16_t* x, int64_t M, const u
         a.scales = m.scales;
         a.x = x + m0 * m.cols;
         a.bias = bias;
-        a.y = y + m0 * m.rows;
+        a.y = y ? y + m0 * m.rows : nullptr;
         a.y32 = y32 ? y32 + m0 * m.rows : nullptr;
+        if (xa) a.xa = *xa;
         a.M = int(M - m0 < 16 ? M - m0 : 16);
         a.N = m.rows;
         a.K = m.cols;
@@ -596,6 +676,7 @@ cudaError_t launch_decode(const Matrix& m, const uint16_t* x, int64_t M, const u
                 break;
         }
         if (e != cudaSuccess) return e;
+        if (xa) xa->fused = a.xa.fused;
     }
     return cudaSuccess;
 }

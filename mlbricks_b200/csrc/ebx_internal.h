@@ -38,12 +38,43 @@ cudaError_t launch_tiles_to_payload(const Matrix& m, uint8_t* payload, uint64_t 
                                     cudaStream_t s);
 cudaError_t launch_materialize(const Matrix& m, uint16_t* out, cudaStream_t s);
 
+// Tensor-parallel exchange region (one per rank, mapped by every rank):
+//   [kXchgCounterOff] uint32: CTAs of the running exchange kernel that are done (local)
+//   [kXchgEpochOff]   uint32: epoch of the last completed exchange (local)
+//   [kXchgDataOff]    uint64 word[2][world][M][N]: partial of source rank r for epoch E
+//                     in slot (E & 1), stored as one 8-byte word {fp32 bits, E}
+// A reader polls a word until its upper half equals the epoch it expects: data
+// and flag arrive in one single-copy-atomic store, so no fence or separate flag
+// is needed (the low-latency protocol of NCCL's LL transport, restated).
+constexpr int kMaxWorld = 8;
+constexpr size_t kXchgCounterOff = 0;
+constexpr size_t kXchgEpochOff = 128;
+constexpr size_t kXchgDataOff = 256;
+
+struct XchgArgs {
+    uint8_t* peer[kMaxWorld];  // every rank's region as mapped here; peer[rank] is our own
+    int world = 0;             // 0: no exchange (plain y / y32 output)
+    int rank = 0;
+    int fused = 0;             // set by the launcher: the decode kernel also reduces (grid co-resident)
+};
+
 // ebx_decode.cu -------------------------------------------------------------
+// With xa (world > 0, M <= 16) the kernel stores its fp32 partials (before
+// bias) into every rank's region for epoch + 1.  If its whole grid can be
+// co-resident it is launched cooperatively with xa->fused = 1 and also waits
+// for all ranks' partials of its own outputs, reduces them, writes y / y32 and
+// advances the epoch; otherwise xa->fused = 0 and launch_xchg_finish must follow.
 cudaError_t launch_decode(const Matrix& m, const uint16_t* x, int64_t M, const uint16_t* bias,
-                          uint16_t* y, float* y32, cudaStream_t s);
+                          uint16_t* y, float* y32, cudaStream_t s, XchgArgs* xa = nullptr);
 // Reads (and optionally clears) the device-side status word that bounded
 // waits set on timeout (0 = healthy).  Synchronizes `s`.
 cudaError_t read_device_status(int* status, bool clear, cudaStream_t s);
+
+// ebx_exchange.cu -----------------------------------------------------------
+// Waits for every rank's partials of epoch + 1, y = fp16(sum_r partial_r + bias), advances the epoch.
+cudaError_t launch_xchg_finish(const XchgArgs& xa, int M, int N, const uint16_t* bias,
+                               uint16_t* y, float* y32, cudaStream_t s);
+cudaError_t read_xchg_status(int* status, bool clear, cudaStream_t s);
 
 // ebx_gemm.cu ---------------------------------------------------------------
 // Rows above which ebx_linear takes the materialise + tcgen05 GEMM route.

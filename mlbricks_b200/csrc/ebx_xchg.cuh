@@ -1,0 +1,109 @@
+// ebx_xchg.cuh -- device side of the tensor-parallel exchange.
+//
+// Every partial travels as one 8-byte word {fp32 bits, epoch} written with a
+// single store into each rank's region (NVLink for peers).  A reader polls the
+// word itself until its upper half equals the epoch it expects, so the value
+// and its readiness arrive together: no fence, no counter and no flag word sit
+// between the producer's store and the consumer's load.  Two slots (epoch & 1)
+// keep a rank that runs one exchange ahead from overwriting words a slower
+// rank has not read yet; it cannot run two ahead, because finishing exchange
+// E + 1 needs every rank's partials of E + 1, which each rank produces only
+// after its own exchange E is complete.
+//
+// The epoch lives in device memory (so CUDA graph replays advance it): every
+// CTA reads it at its start, and the last CTA of the kernel that completes an
+// exchange (the fused decode kernel, or the finish kernel) stores epoch + 1.
+#pragma once
+
+#include <stdint.h>
+
+#include "ebx_internal.h"
+
+namespace ebx {
+
+constexpr int kXchgTimeout = 0x7102;
+constexpr uint64_t kXchgWaitNs = 2000000000ull;  // 2 s per exchange wait
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Epoch of the last completed exchange of this rank.
+__device__ __forceinline__ uint32_t xchg_epoch(const XchgArgs& xa) {
+    return *reinterpret_cast<volatile const uint32_t*>(xa.peer[xa.rank] + kXchgEpochOff);
+}
+
+// Words of source rank `src` for epoch `e` inside a region: [M][N].
+__device__ __forceinline__ uint64_t* xchg_words(uint8_t* region, uint32_t e, int world, int src,
+                                                int M, int N) {
+    return reinterpret_cast<uint64_t*>(region + kXchgDataOff) +
+           (size_t(e & 1u) * size_t(world) + size_t(src)) * size_t(M) * size_t(N);
+}
+
+// Store this rank's partial of (tok, row) for epoch e into every rank's region.
+__device__ __forceinline__ void xchg_push(const XchgArgs& xa, uint32_t e, int M, int N, int tok,
+                                          int row, float v) {
+    const uint64_t w = (uint64_t(e) << 32) | uint64_t(__float_as_uint(v));
+    const size_t off = size_t(tok) * size_t(N) + size_t(row);
+#pragma unroll 1
+    for (int q = 0; q < xa.world; ++q)
+        st_relaxed_sys_u64(xchg_words(xa.peer[q], e, xa.world, xa.rank, M, N) + off, w);
+}
+
+// Sum of all ranks' partials of (tok, row) for epoch e, in rank order 0..world-1
+// (the same order on every rank, so every rank holds the same bits).  Polls each
+// word until it carries epoch e; false if one did not arrive within the limit.
+__device__ __forceinline__ bool xchg_gather(const XchgArgs& xa, uint32_t e, int M, int N, int tok,
+                                            int row, float& out) {
+    uint8_t* own = xa.peer[xa.rank];
+    const size_t off = size_t(tok) * size_t(N) + size_t(row);
+    float s = 0.0f;
+    uint64_t t0 = 0;
+#pragma unroll 1
+    for (int r = 0; r < xa.world; ++r) {
+        const uint64_t* p = xchg_words(own, e, xa.world, r, M, N) + off;
+        uint64_t w = ld_relaxed_sys_u64(p);
+        while (uint32_t(w >> 32) != e) {
+            const uint64_t now = global_ns();
+            if (t0 == 0) {
+                t0 = now;
+            } else if (now - t0 > kXchgWaitNs) {
+                return false;
+            }
+            __nanosleep(16);
+            w = ld_relaxed_sys_u64(p);
+        }
+        const float v = __uint_as_float(uint32_t(w));
+        s = r == 0 ? v : s + v;
+    }
+    out = s;
+    return true;
+}
+
+// Every thread calls this at the very end of the kernel that completes exchange
+// e; the last CTA to arrive stores the new epoch (all CTAs read the old one at
+// their start, before arriving).
+__device__ __forceinline__ void xchg_advance(const XchgArgs& xa, uint32_t e) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t* counter = reinterpret_cast<uint32_t*>(xa.peer[xa.rank] + kXchgCounterOff);
+        if (atomicAdd(counter, 1u) + 1u == gridDim.x) {
+            atomicExch(counter, 0u);
+            *reinterpret_cast<volatile uint32_t*>(xa.peer[xa.rank] + kXchgEpochOff) = e;
+        }
+    }
+}
+
+}  // namespace ebx

@@ -388,6 +388,29 @@ class RuntimeMatrix:
             self._launch(xc, M, b, y, y32)
         return (y, y32) if out32 else y
 
+    def linear_allreduce(self, x: torch.Tensor, exchange, bias: torch.Tensor | None = None,
+                         out32: bool = False):
+        """Row-parallel shard + all-reduce in one libebx call (ebx_linear_allreduce):
+        y = fp16(sum over ranks of x_r @ W_r^T + bias); x is this rank's K slice."""
+        if not x.is_cuda or x.dtype != torch.float16:
+            raise ValueError("linear_allreduce requires FP16 CUDA activations")
+        if x.shape[-1] != self._cols:
+            raise ValueError(f"expected last dimension {self._cols}, got {x.shape[-1]}")
+        xc = x.contiguous()
+        M = xc.numel() // self._cols
+        y = torch.empty((*x.shape[:-1], self._rows), dtype=torch.float16, device=x.device)
+        y32 = torch.empty(y.shape, dtype=torch.float32, device=x.device) if out32 else None
+        b = None
+        if bias is not None:
+            b = bias.detach().to(device=x.device, dtype=torch.float16).contiguous()
+            if b.numel() != self._rows:
+                raise ValueError("bias must match output features")
+        with torch.cuda.device(self._device):
+            _ebx.check(_LIB.ebx_linear_allreduce(
+                self._h, xc.data_ptr(), M, None if b is None else b.data_ptr(), y.data_ptr(),
+                None if y32 is None else y32.data_ptr(), exchange.handle, _stream()))
+        return (y, y32) if out32 else y
+
     def forwardTorch(self, input: torch.Tensor) -> torch.Tensor:
         if not input.is_cuda:
             raise ValueError("forwardTorch requires a CUDA tensor")

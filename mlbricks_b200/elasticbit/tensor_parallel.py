@@ -17,6 +17,12 @@ Everything here is host orchestration; the per-rank compute is libebx
 (``RuntimeMatrix.linear``).  The collective is pluggable (``allreduce`` /
 ``allgather`` callables) so the orchestration can be exercised with gloo ranks on
 CPU and a stand-in compute function.
+
+For decode-sized inputs (M <= 16) a row-parallel layer can skip the collective
+altogether: with an :class:`Exchange` attached, one libebx call
+(``ebx_linear_allreduce``) runs the shard's decode kernel, which stores its fp32
+partials straight into every rank's exchange region over NVLink, and a finish
+kernel that waits for all ranks' epoch flags and sums the partials in rank order.
 """
 from __future__ import annotations
 
@@ -78,6 +84,67 @@ class Collectives:
         return Collectives(allreduce, allgather)
 
 
+class Exchange:
+    """This rank's libebx tensor-parallel exchange (``ebx_exchange_*``).
+
+    ``allgather_bytes(blob) -> [blob of rank 0, ..., blob of rank world-1]`` is the
+    host transport for the opaque handles (``from_group`` uses torch.distributed).
+    Close it only after every rank has finished its last exchange (a barrier):
+    peers write into this rank's region until then.
+    """
+
+    def __init__(self, max_m: int, max_n: int, world: int, rank: int, device: int,
+                 allgather_bytes: Callable[[bytes], list]) -> None:
+        import ctypes
+
+        from .. import _ebx
+
+        self._lib = _ebx.load()
+        self.max_m, self.max_n, self.world, self.rank = int(max_m), int(max_n), int(world), int(rank)
+        blob = (ctypes.c_uint8 * _ebx.EXCHANGE_HANDLE_BYTES)()
+        h = ctypes.c_void_p()
+        _ebx.check(self._lib.ebx_exchange_create(world, rank, device, max_m, max_n, blob,
+                                                 ctypes.byref(h)))
+        self.handle = h
+        blobs = allgather_bytes(bytes(blob))
+        if len(blobs) != world or any(len(b) != _ebx.EXCHANGE_HANDLE_BYTES for b in blobs):
+            self.close()
+            raise RuntimeError("exchange handle all-gather returned malformed blobs")
+        try:
+            _ebx.check(self._lib.ebx_exchange_connect(h, b"".join(blobs)))
+        except Exception:
+            self.close()
+            raise
+
+    @staticmethod
+    def from_group(max_m: int, max_n: int, group=None) -> "Exchange":
+        import torch.distributed as dist
+
+        world = dist.get_world_size(group)
+
+        def allgather_bytes(b: bytes) -> list:
+            out = [None] * world
+            dist.all_gather_object(out, b, group=group)
+            return out
+
+        ex = Exchange(max_m, max_n, world, dist.get_rank(group), torch.cuda.current_device(),
+                      allgather_bytes)
+        dist.barrier(group)  # every rank has mapped every region before the first use
+        return ex
+
+    def close(self) -> None:
+        h = getattr(self, "handle", None)
+        if h is not None and h.value:
+            self._lib.ebx_exchange_destroy(h)
+            self.handle = None
+
+    def __del__(self) -> None:  # pragma: no cover - interpreter teardown order
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class ShardedLinear(torch.nn.Module):
     """One rank's part of a tensor-parallel compressed linear.
 
@@ -89,7 +156,8 @@ class ShardedLinear(torch.nn.Module):
                  bounds: tuple[int, int], bias: torch.Tensor | None = None,
                  collectives: Collectives | None = None,
                  local: Callable[[torch.Tensor, bool], torch.Tensor] | None = None,
-                 gather: bool = False, input_is_local: bool = False) -> None:
+                 gather: bool = False, input_is_local: bool = False,
+                 exchange: Exchange | None = None) -> None:
         super().__init__()
         if mode not in MODES:
             raise ValueError(f"mode must be one of {MODES}")
@@ -101,6 +169,7 @@ class ShardedLinear(torch.nn.Module):
         self.gather = bool(gather)
         self.input_is_local = bool(input_is_local)  # row mode: x already holds this K slice
         self.collectives = collectives
+        self.exchange = exchange  # row mode, M <= exchange.max_m: ebx_linear_allreduce
         self._local = local
         if bias is None:
             self.register_parameter("bias", None)
@@ -134,6 +203,10 @@ class ShardedLinear(torch.nn.Module):
         # row parallel: x is the full activation; use this rank's K slice
         lo, hi = self.bounds
         xs = x.contiguous() if self.input_is_local else x[..., lo:hi].contiguous()
+        ex = self.exchange
+        if ex is not None and self._local is None and xs.numel() // max(1, xs.shape[-1]) <= ex.max_m:
+            native = getattr(self.matrix, "_native", self.matrix)
+            return native.linear_allreduce(xs, ex, bias=self.bias)
         part = self._compute(xs, True, None)
         if self.collectives is not None:
             self.collectives.allreduce(part)
@@ -145,7 +218,7 @@ class ShardedLinear(torch.nn.Module):
 def build_sharded(codes, scales, bits: int, mode: str, world: int, rank: int, *,
                   threshold: float = 0.0, error: float = 0.0, bias=None,
                   collectives: Collectives | None = None, gather: bool = False,
-                  input_is_local: bool = False,
+                  input_is_local: bool = False, exchange: Exchange | None = None,
                   decodePolicy: str = "fullPrecision") -> ShardedLinear:
     """Create this rank's shard (libebx matrix) from the global analyzer result."""
     from .core import RuntimeMatrix
@@ -159,7 +232,37 @@ def build_sharded(codes, scales, bits: int, mode: str, world: int, rank: int, *,
     m = RuntimeMatrix._compressSelectedCodes(c, s, bits, threshold, error,
                                              decodePolicy=decodePolicy)
     return ShardedLinear(m, mode, N, K, bounds, bias=bias, collectives=collectives, gather=gather,
-                         input_is_local=input_is_local)
+                         input_is_local=input_is_local, exchange=exchange if mode == "row" else None)
 
 
-__all__ = ["MODES", "shard_bounds", "shard_codes", "Collectives", "ShardedLinear", "build_sharded"]
+def build_column_fused(parts, bits: int, world: int, rank: int, *, threshold: float = 0.0,
+                       error: float = 0.0, decodePolicy: str = "fullPrecision") -> ShardedLinear:
+    """One column-parallel shard holding this rank's rows of several matrices that
+    read the same input and share a storage width (gate and up; Q, K and V): the
+    rank's slice of each part, concatenated along rows, so one decode launch serves
+    them all.  The local output is [part 0 slice | part 1 slice | ...]."""
+    from .core import RuntimeMatrix
+
+    cs, ss, widths = [], [], []
+    K = int(parts[0][0].shape[1])
+    for codes, scales in parts:
+        if int(codes.shape[1]) != K:
+            raise ValueError("fused column parts must share in_features")
+        c, s, (lo, hi) = shard_codes(codes, scales, "column", world, rank)
+        cs.append(c)
+        ss.append(s)
+        widths.append(hi - lo)
+    if torch.is_tensor(cs[0]):
+        c = torch.cat([t.contiguous() for t in cs], 0).contiguous()
+        s = torch.cat([torch.as_tensor(t) for t in ss], 0).contiguous()
+    else:
+        c = np.ascontiguousarray(np.concatenate(cs, 0))
+        s = np.ascontiguousarray(np.concatenate(ss, 0))
+    m = RuntimeMatrix._compressSelectedCodes(c, s, bits, threshold, error, decodePolicy=decodePolicy)
+    lin = ShardedLinear(m, "column", int(c.shape[0]), K, (0, int(c.shape[0])))
+    lin.part_widths = widths
+    return lin
+
+
+__all__ = ["MODES", "shard_bounds", "shard_codes", "Collectives", "Exchange", "ShardedLinear",
+           "build_sharded", "build_column_fused"]

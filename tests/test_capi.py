@@ -59,3 +59,19 @@ def test_argument_errors_without_gpu():
         _ebx.check(_ebx.EBX_ERR_INVALID)
     with pytest.raises(RuntimeError):
         _ebx.check(_ebx.EBX_ERR_CUDA)
+
+
+def test_exchange_argument_errors_without_gpu():
+    lib = _ebx.load()
+    h = ctypes.c_void_p()
+    blob = (ctypes.c_uint8 * _ebx.EXCHANGE_HANDLE_BYTES)()
+    # shape and rank checks come before any CUDA call
+    assert lib.ebx_exchange_create(9, 0, 0, 1, 16, blob, ctypes.byref(h)) == _ebx.EBX_ERR_INVALID
+    assert "world" in _ebx.last_error()
+    assert lib.ebx_exchange_create(2, 2, 0, 1, 16, blob, ctypes.byref(h)) == _ebx.EBX_ERR_INVALID
+    assert lib.ebx_exchange_create(2, 0, 0, 17, 16, blob, ctypes.byref(h)) == _ebx.EBX_ERR_INVALID
+    assert "max_m" in _ebx.last_error()
+    assert lib.ebx_exchange_create(2, 0, 0, 1, 16, None, ctypes.byref(h)) == _ebx.EBX_ERR_INVALID
+    assert lib.ebx_exchange_connect(None, blob) == _ebx.EBX_ERR_INVALID
+    assert lib.ebx_exchange_destroy(None) == _ebx.EBX_OK
+    assert lib.ebx_linear_allreduce(None, None, 1, None, None, None, None, None) == _ebx.EBX_ERR_INVALID

@@ -1,5 +1,10 @@
-"""Tensor-parallel shards on 2+ GPUs over NCCL (libebx compute per rank) vs the
-unsharded matrix on one GPU.  Skipped when fewer than two GPUs are visible."""
+"""Tensor-parallel shards on 2+ GPUs (one process per GPU, NCCL for the host
+plumbing, libebx compute) against the unsharded matrix on one GPU, for both
+all-reduce routes of row-parallel layers: NCCL over fp32 partials, and the
+libebx exchange (ebx_linear_allreduce).  Also: a rank that never joins an
+exchange makes the others' finish kernel give up after its bounded wait and
+report it through ebx_device_status, with the CUDA context still usable.
+Skipped when fewer than two GPUs are visible."""
 from __future__ import annotations
 
 import os
@@ -11,6 +16,9 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
+SHAPE = (512, 4096, 10)  # N, K, bits
+MS = (1, 5, 16, 100)
+
 
 def _free_port() -> int:
     with socket.socket() as sk:
@@ -18,74 +26,159 @@ def _free_port() -> int:
         return sk.getsockname()[1]
 
 
-def _worker(rank, world, port, q_out):
+def _case():
+    from oracle import oracle as O
+
+    N, K, bits = SHAPE
+    w = O.baseline_weights(N, K, seed=11)
+    s = O.row_scales(w, bits)
+    q = O.quantize(w, s, bits)
+    bias = O.normal((N,), seed=12, scale=0.1).astype(np.float16)
+    xs = {M: O.normal((M, K), seed=M).astype(np.float16) for M in MS}
+    return q, s, bits, bias, xs
+
+
+def _init(rank, world, port):
     import datetime
 
     import torch.distributed as dist
 
-    from mlbricks_b200.elasticbit import tensor_parallel as tp
-    from oracle import oracle as O
-
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
+    return dist
+
+
+def _worker(rank, world, port, q_out):
+    dist = _init(rank, world, port)
+    from mlbricks_b200.elasticbit import tensor_parallel as tp
+
     try:
-        N, K, bits = 512, 4096, 10
-        w = O.baseline_weights(N, K, seed=11)
-        s = O.row_scales(w, bits)
-        q = O.quantize(w, s, bits)
-        bias = torch.from_numpy(O.normal((N,), seed=12, scale=0.1)).cuda()
+        q, s, bits, bias, xs = _case()
+        bias_t = torch.from_numpy(bias).cuda()
         coll = tp.Collectives.from_group()
+        ex = tp.Exchange.from_group(16, 4096)
         res = {}
-        for M in (1, 16, 100):
-            x = torch.from_numpy(O.normal((M, K), seed=M).astype(np.float16)).cuda()
+        lin = {mode: tp.build_sharded(q, s, bits, mode, world, rank, bias=bias_t,
+                                      collectives=coll, gather=True) for mode in tp.MODES}
+        lin_x = tp.build_sharded(q, s, bits, "row", world, rank, bias=bias_t, collectives=coll,
+                                 exchange=ex)
+        for M in MS:
+            x = torch.from_numpy(xs[M]).cuda()
             for mode in tp.MODES:
-                lin = tp.build_sharded(q, s, bits, mode, world, rank, bias=bias,
-                                       collectives=coll, gather=True)
-                res[(M, mode)] = lin(x).float().cpu().numpy()
+                res[(M, mode)] = lin[mode](x).float().cpu().numpy()
+            for rep in range(3):  # successive epochs
+                res[(M, "exchange", rep)] = lin_x(x).float().cpu().numpy()
+        torch.cuda.synchronize()
+        import ctypes
+
+        from mlbricks_b200 import _ebx
+        lib = _ebx.load()
+        v = ctypes.c_int32()
+        _ebx.check(lib.ebx_device_status(rank, ctypes.byref(v), 0))
+        res["status"] = int(v.value)
+        dist.barrier()
+        ex.close()
         q_out.put((rank, res))
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-def test_tensor_parallel_matches_single_gpu(cuda_ok):
+def _unsharded_reference():
+    from mlbricks_b200 import RuntimeMatrix
+
+    q, s, bits, bias, xs = _case()
+    full = RuntimeMatrix._compressSelectedCodes(q, s, bits, 0.0, 0.0, decodePolicy="fullPrecision")
+    b = torch.from_numpy(bias).cuda()
+    return {M: full.linear(torch.from_numpy(xs[M]).cuda(), b).float().cpu().numpy() for M in MS}
+
+
+def _spawn(target, world, timeout=300):
     import torch.multiprocessing as mp
 
-    from mlbricks_b200 import RuntimeMatrix
-    from oracle import oracle as O
-
-    world = torch.cuda.device_count()
-    if world < 2:
-        pytest.skip("needs at least two GPUs")
-    world = min(world, 8)
     ctx = mp.get_context("spawn")
     q_out = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q_out)) for r in range(world)]
+    procs = [ctx.Process(target=target, args=(r, world, port, q_out)) for r in range(world)]
     for p in procs:
         p.start()
-    results = dict(q_out.get(timeout=300) for _ in range(world))
+    results = dict(q_out.get(timeout=timeout) for _ in range(world))
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    N, K, bits = 512, 4096, 10
-    w = O.baseline_weights(N, K, seed=11)
-    s = O.row_scales(w, bits)
-    q = O.quantize(w, s, bits)
-    bias = torch.from_numpy(O.normal((N,), seed=12, scale=0.1)).cuda().half()
-    full = RuntimeMatrix._compressSelectedCodes(q, s, bits, 0.0, 0.0, decodePolicy="fullPrecision")
-    for M in (1, 16, 100):
-        x = torch.from_numpy(O.normal((M, K), seed=M).astype(np.float16)).cuda()
-        ref = full.linear(x, bias).float().cpu().numpy()
+    return results
+
+
+def test_tensor_parallel_matches_single_gpu(cuda_ok):
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("needs at least two GPUs")
+    results = _spawn(_worker, world)
+    ref = _unsharded_reference()
+    for M in MS:
+        r16 = ref[M].astype(np.float16)
+        tol = np.maximum(2e-3, np.spacing(np.abs(r16)).astype(np.float32))
         for rank in range(world):
+            res = results[rank]
+            assert res["status"] == 0
             for mode in ("column", "row"):
-                y = results[rank][(M, mode)]
-                ulp = np.spacing(np.abs(ref.astype(np.float16))).astype(np.float32)
-                assert np.all(np.abs(y - ref) <= np.maximum(2e-3, ulp)), (M, mode, rank)
+                y = res[(M, mode)]
+                assert np.all(np.abs(y - ref[M]) <= tol), (M, mode, rank)
                 if mode == "column":
-                    assert np.array_equal(y, ref)  # same kernel, same rows: bit-identical
+                    assert np.array_equal(y, ref[M])  # same kernel, same rows: bit-identical
+            if M <= 16:
+                y0 = res[(M, "exchange", 0)]
+                assert np.all(np.abs(y0 - ref[M]) <= tol), (M, "exchange", rank)
+                for rep in (1, 2):
+                    assert np.array_equal(res[(M, "exchange", rep)], y0)
+                # rank-order summation: every rank holds the same bits
+                assert np.array_equal(y0, results[0][(M, "exchange", 0)])
+
+
+def _absent_rank_worker(rank, world, port, q_out):
+    dist = _init(rank, world, port)
+    import ctypes
+
+    from mlbricks_b200 import _ebx
+    from mlbricks_b200.elasticbit import tensor_parallel as tp
+
+    try:
+        q, s, bits, bias, xs = _case()
+        ex = tp.Exchange.from_group(16, 4096)
+        lin = tp.build_sharded(q, s, bits, "row", world, rank, exchange=ex)
+        out = {}
+        lib = _ebx.load()
+        v = ctypes.c_int32()
+        if rank == 0:
+            # ranks >= 1 never join this exchange: the finish kernel's bounded wait
+            # (about 2 s) gives up and records the failure
+            x = torch.from_numpy(xs[1]).cuda()
+            lin(x)
+            torch.cuda.synchronize()
+            _ebx.check(lib.ebx_device_status(rank, ctypes.byref(v), 1))
+            out["status"] = int(v.value)
+            # the context is still usable: a plain launch works and the status is clear
+            y = lin.matrix.linear(x[:, : lin.bounds[1] - lin.bounds[0]].contiguous())
+            torch.cuda.synchronize()
+            out["after"] = bool(torch.isfinite(y.float()).all().item())
+            _ebx.check(lib.ebx_device_status(rank, ctypes.byref(v), 0))
+            out["status_after"] = int(v.value)
+        dist.barrier()
+        ex.close()  # out of step now: discarded, as the header says
+        q_out.put((rank, out))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_exchange_reports_absent_rank(cuda_ok):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs at least two GPUs")
+    results = _spawn(_absent_rank_worker, 2)
+    assert results[0]["status"] == 0x7102
+    assert results[0]["after"] and results[0]["status_after"] == 0
