@@ -204,6 +204,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Every mbarrier wait in libebx is bounded in wall-clock time (a try_wait probe
+// may itself suspend the thread for a while, so a probe count alone is not a
+// bound): after kMbarWaitNs the caller gets false and must record an error,
+// skip the work that depended on the barrier and leave.
+constexpr uint64_t kMbarWaitNs = 2000000000ull;  // 2 s
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+    for (int i = 0; i < 64; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        for (int i = 0; i < 256; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (global_ns() - t0 > kMbarWaitNs) return false;
+    }
+}
+
 // Global -> shared bulk copy completing on an mbarrier.  src/dst 16-byte
 // aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,

@@ -37,7 +37,6 @@ constexpr int kThreads = kWarps * 32;
 // Device health word: bounded waits that give up record their code here.
 __device__ int g_device_status = 0;
 constexpr int kDeviceTimeout = 0x7101;
-constexpr uint32_t kWaitLimit = 1u << 24;
 
 struct DecodeArgs {
     const uint8_t* tiles;
@@ -263,9 +262,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
 // bounded) and leaves the loop, so a stuck copy cannot hang the GPU.
 
 __device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity) {
-    for (uint32_t it = 0; it < kWaitLimit; ++it)
-        if (mbar_try_wait(bar, parity)) return true;
-    return false;
+    return mbar_wait_bounded(bar, parity);  // wall-clock bound (ebx_common.cuh)
 }
 
 // ---------------------------------------------------------------------------

@@ -37,7 +37,6 @@ constexpr int kBBytes = BN * BK * 2;
 constexpr int kStageBytesG = kABytes + kBBytes;
 constexpr int kTmemCols = 256;
 constexpr int kGemmThreads = 128;
-constexpr uint32_t kGemmWaitLimit = 1u << 22;
 
 // instruction descriptor: D fp32, A/B fp16, both K-major, N = 256, M = 128
 constexpr uint32_t kIdesc = (1u << 4) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
@@ -63,9 +62,8 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 }
 
 __device__ __forceinline__ bool gemm_wait(uint32_t bar, uint32_t parity) {
-    for (uint32_t it = 0; it < kGemmWaitLimit; ++it)
-        if (mbar_try_wait(bar, parity)) return true;
-    atomicExch(&g_gemm_status, 0x7102);
+    if (mbar_wait_bounded(bar, parity)) return true;
+    atomicExch(&g_gemm_status, 0x7103);
     return false;
 }
 

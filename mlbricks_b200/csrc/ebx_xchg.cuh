@@ -17,18 +17,13 @@
 
 #include <stdint.h>
 
+#include "ebx_common.cuh"
 #include "ebx_internal.h"
 
 namespace ebx {
 
 constexpr int kXchgTimeout = 0x7102;
 constexpr uint64_t kXchgWaitNs = 2000000000ull;  // 2 s per exchange wait
-
-__device__ __forceinline__ uint64_t global_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
 
 __device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
     asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");

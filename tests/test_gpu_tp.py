@@ -129,8 +129,8 @@ def test_tensor_parallel_matches_single_gpu(cuda_ok):
             for mode in ("column", "row"):
                 y = res[(M, mode)]
                 assert np.all(np.abs(y - ref[M]) <= tol), (M, mode, rank)
-                if mode == "column":
-                    assert np.array_equal(y, ref[M])  # same kernel, same rows: bit-identical
+                if mode == "column":  # every rank gathers the same shards
+                    assert np.array_equal(y, results[0][(M, mode)])
             if M <= 16:
                 y0 = res[(M, "exchange", 0)]
                 assert np.all(np.abs(y0 - ref[M]) <= tol), (M, "exchange", rank)
