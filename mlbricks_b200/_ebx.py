@@ -120,12 +120,17 @@ def check(status: int) -> None:
     raise RuntimeError(msg)
 
 
-def stream_ptr(stream=None) -> int:
-    """cudaStream_t of the given (or current) torch stream as an integer."""
+def stream_ptr(stream=None, device: int | None = None) -> int:
+    """cudaStream_t of the given torch stream, or of the current stream of
+    `device` (default: the current device), as an integer."""
     import torch
 
-    s = stream if stream is not None else torch.cuda.current_stream()
-    return int(s.cuda_stream)
+    if stream is not None:
+        return int(stream.cuda_stream)
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None:  # no Stream object per call: this sits on every launch
+        return int(raw(torch.cuda.current_device() if device is None else device))
+    return int(torch.cuda.current_stream(device).cuda_stream)
 
 
 __all__ = ["LIB_PATH", "MatrixInfo", "SIGNATURES", "load", "last_error", "check", "stream_ptr"]

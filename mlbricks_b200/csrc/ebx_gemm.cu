@@ -6,16 +6,20 @@
 // RuntimeMatrix holds for its W16 path) is written to the caller's workspace by
 // ebx_pack.cu's materialize kernel, then this kernel computes
 //     y[m, n] = fp16( sum_k x[m,k] * W16[n,k] + bias[n] )
-// with 5th-generation tensor cores:
-//   * CTA tile 128 (tokens, MMA M) x 256 (weight rows, MMA N), K step 64;
-//   * TMA (cp.async.bulk.tensor, 128-byte swizzle, no multicast) loads the
-//     x and W16 tiles into a 4-stage shared-memory ring;
-//   * one thread issues tcgen05.mma (kind::f16, fp32 accumulate) into a
-//     128 x 256 fp32 accumulator in tensor memory; tcgen05.commit frees each
-//     stage when the MMAs reading it complete;
-//   * four warps read the accumulator back with tcgen05.ld (warp w owns TMEM
-//     lanes 32w..32w+31 = tokens), add the bias in fp32 and store fp16 (+fp32).
-// Every mbarrier wait is bounded; a timeout sets the device status word.
+// with 5th-generation tensor cores, as a persistent kernel (one CTA per SM):
+//   * output tiles 128 (tokens, MMA M) x 256 (weight rows, MMA N), K step 64,
+//     visited in groups of kGroupM token tiles per weight tile so that the
+//     tiles in flight on the whole GPU share an L2-resident slice of x and W16;
+//   * warp 0: TMA producer (cp.async.bulk.tensor, 128-byte swizzle, no
+//     multicast) into a 4-stage shared-memory ring, running ahead across tiles;
+//   * warp 1: one thread issues tcgen05.mma (kind::f16, fp32 accumulate) into
+//     one of two 128 x 256 fp32 accumulators in tensor memory (512 columns)
+//     and tcgen05.commit frees each ring stage, then marks the accumulator full;
+//   * warps 2-5: epilogue -- tcgen05.ld of TMEM lanes 32(w%4)..+31 (tokens),
+//     bias in fp32, fp16 (+fp32) stores, then the accumulator is released --
+//     while the MMAs of the next tile run into the other accumulator.
+// Every mbarrier wait is bounded in time; a timeout sets the device status word
+// and the roles leave their loops.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -35,8 +39,10 @@ constexpr int kStagesG = 4;
 constexpr int kABytes = BM * BK * 2;
 constexpr int kBBytes = BN * BK * 2;
 constexpr int kStageBytesG = kABytes + kBBytes;
-constexpr int kTmemCols = 256;
-constexpr int kGemmThreads = 128;
+constexpr int kAccCols = BN;             // one fp32 accumulator: 128 lanes x 256 columns
+constexpr int kTmemCols = 2 * kAccCols;  // double-buffered
+constexpr int kGemmThreads = 192;        // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int kGroupM = 8;               // token tiles per raster group
 
 // instruction descriptor: D fp32, A/B fp16, both K-major, N = 256, M = 128
 constexpr uint32_t kIdesc = (1u << 4) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
@@ -91,6 +97,18 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
                  : "memory");
 }
 
+// Output tile t -> (token tile, weight tile): groups of kGroupM token tiles walk
+// the weight tiles together, so concurrently resident CTAs share operands in L2.
+__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& mt, int& nt) {
+    const int per_group = kGroupM * n_tiles;
+    const int grp = t / per_group;
+    const int first = grp * kGroupM;
+    const int gm = m_tiles - first < kGroupM ? m_tiles - first : kGroupM;
+    const int idx = t - grp * per_group;
+    mt = first + idx % gm;
+    nt = idx / gm;
+}
+
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_x, const __grid_constant__ CUtensorMap tma_w,
                     GemmArgs a) {
@@ -99,14 +117,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                                ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStagesG * kStageBytesG);
     uint64_t* empty = full + kStagesG;
-    uint64_t* done = empty + kStagesG;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint64_t* acc_full = empty + kStagesG;
+    uint64_t* acc_empty = acc_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN;
-    const int m0 = blockIdx.y * BM;
     const int kblocks = (a.K + BK - 1) / BK;
+    const int m_tiles = (a.M + BM - 1) / BM;
+    const int n_tiles = (a.N + BN - 1) / BN;
+    const int tiles = m_tiles * n_tiles;
 
     if (warp == 0) {
         if (lane == 0) {
@@ -114,7 +134,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 mbar_init(smem_u32(&full[i]), 1);
                 mbar_init(smem_u32(&empty[i]), 1);
             }
-            mbar_init(smem_u32(done), 1);
+            for (int i = 0; i < 2; ++i) {
+                mbar_init(smem_u32(&acc_full[i]), 1);
+                mbar_init(smem_u32(&acc_empty[i]), 4);  // one arrival per epilogue warp
+            }
             fence_proxy_async_smem();
         }
         __syncwarp();
@@ -130,96 +153,126 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
-        if (lane == 0) {  // TMA producer
-            for (int kb = 0; kb < kblocks; ++kb) {
-                const int st = kb % kStagesG;
-                if (kb >= kStagesG &&
-                    !gemm_wait(smem_u32(&empty[st]), uint32_t(((kb / kStagesG) - 1) & 1)))
-                    break;
-                const uint32_t bar = smem_u32(&full[st]);
-                mbar_expect_tx(bar, kStageBytesG);
-                uint8_t* stage = smem + st * kStageBytesG;
-                tma_load_2d(smem_u32(stage), &tma_x, kb * BK, m0, bar);
-                tma_load_2d(smem_u32(stage + kABytes), &tma_w, kb * BK, n0, bar);
+        if (lane == 0) {  // TMA producer: runs ahead across tiles
+            int it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                int mt, nt;
+                tile_coords(t, m_tiles, n_tiles, mt, nt);
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int st = it % kStagesG;
+                    if (it >= kStagesG &&
+                        !gemm_wait(smem_u32(&empty[st]), uint32_t(((it / kStagesG) - 1) & 1))) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t bar = smem_u32(&full[st]);
+                    mbar_expect_tx(bar, kStageBytesG);
+                    uint8_t* stage = smem + st * kStageBytesG;
+                    tma_load_2d(smem_u32(stage), &tma_x, kb * BK, mt * BM, bar);
+                    tma_load_2d(smem_u32(stage + kABytes), &tma_w, kb * BK, nt * BN, bar);
+                }
             }
         }
         __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {  // MMA issuer
+            int it = 0, i = 0;
             bool ok = true;
-            for (int kb = 0; kb < kblocks && ok; ++kb) {
-                const int st = kb % kStagesG;
-                ok = gemm_wait(smem_u32(&full[st]), uint32_t((kb / kStagesG) & 1));
-                if (!ok) break;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++i) {
+                const int acc = i & 1;
+                if (i >= 2 && !gemm_wait(smem_u32(&acc_empty[acc]), uint32_t(((i >> 1) - 1) & 1))) break;
                 asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-                const uint32_t abase = smem_u32(smem + st * kStageBytesG);
-                const uint32_t bbase = abase + kABytes;
+                const uint32_t d = tmem + uint32_t(acc * kAccCols);
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int st = it % kStagesG;
+                    if (!gemm_wait(smem_u32(&full[st]), uint32_t((it / kStagesG) & 1))) {
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+                    const uint32_t abase = smem_u32(smem + st * kStageBytesG);
+                    const uint32_t bbase = abase + kABytes;
 #pragma unroll
-                for (int k = 0; k < BK / 16; ++k)
-                    umma_f16(tmem, sw128_desc(abase + k * 32), sw128_desc(bbase + k * 32),
-                             (kb | k) != 0 ? 1u : 0u);
-                umma_commit(smem_u32(&empty[st]));
+                    for (int k = 0; k < BK / 16; ++k)
+                        umma_f16(d, sw128_desc(abase + k * 32), sw128_desc(bbase + k * 32),
+                                 (kb | k) != 0 ? 1u : 0u);
+                    umma_commit(smem_u32(&empty[st]));
+                }
+                umma_commit(smem_u32(&acc_full[acc]));  // fires when this tile's MMAs are done
             }
-            umma_commit(smem_u32(done));  // fires when every MMA above has completed
         }
         __syncwarp();
-    }
-
-    // ---------------- epilogue: TMEM -> registers -> global ----------------
-    const bool ready = gemm_wait(smem_u32(done), 0u);
-    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-    const int m = m0 + warp * 32 + lane;
-    const bool vec = (a.N % 8) == 0;
+    } else {
+        // ---------------- epilogue: TMEM -> registers -> global ----------------
+        const int quarter = warp & 3;  // TMEM lanes this warp may access
+        const bool vec = (a.N % 8) == 0;
+        int i = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+            const int acc = i & 1;
+            if (!gemm_wait(smem_u32(&acc_full[acc]), uint32_t((i >> 1) & 1))) break;
+            asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+            int mt, nt;
+            tile_coords(t, m_tiles, n_tiles, mt, nt);
+            const int m = mt * BM + quarter * 32 + lane;
+            const int n0 = nt * BN;
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-        uint32_t v[32];
-        const uint32_t taddr = tmem + (uint32_t(warp * 32) << 16) + uint32_t(c * 32);
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-            "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
-            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-              "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
-              "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]),
-              "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
-              "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]),
-              "=r"(v[31])
-            : "r"(taddr));
-        asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
-        const int nb = n0 + c * 32;
-        if (!ready || m >= a.M || nb >= a.N) continue;
-        float f[32];
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t v[32];
+                const uint32_t taddr =
+                    tmem + (uint32_t(quarter * 32) << 16) + uint32_t(acc * kAccCols + c * 32);
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+                    "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+                    : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
+                      "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]),
+                      "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]),
+                      "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+                      "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]),
+                      "=r"(v[30]), "=r"(v[31])
+                    : "r"(taddr));
+                asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+                const int nb = n0 + c * 32;
+                if (m >= a.M || nb >= a.N) continue;
+                float f[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            f[j] = __uint_as_float(v[j]);
-            if (a.bias && nb + j < a.N) f[j] += __half2float(__ushort_as_half(a.bias[nb + j]));
-        }
-        uint16_t* yrow = a.y + size_t(m) * a.N + nb;
-        if (vec && nb + 32 <= a.N) {
+                for (int j = 0; j < 32; ++j) {
+                    f[j] = __uint_as_float(v[j]);
+                    if (a.bias && nb + j < a.N) f[j] += __half2float(__ushort_as_half(a.bias[nb + j]));
+                }
+                uint16_t* yrow = a.y + size_t(m) * a.N + nb;
+                if (vec && nb + 32 <= a.N) {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                uint4 pk;
-                pk.x = pack_half2(f[8 * q + 0], f[8 * q + 1]);
-                pk.y = pack_half2(f[8 * q + 2], f[8 * q + 3]);
-                pk.z = pack_half2(f[8 * q + 4], f[8 * q + 5]);
-                pk.w = pack_half2(f[8 * q + 6], f[8 * q + 7]);
-                reinterpret_cast<uint4*>(yrow)[q] = pk;
-            }
-            if (a.y32) {
-                float* y32row = a.y32 + size_t(m) * a.N + nb;
+                    for (int q = 0; q < 4; ++q) {
+                        uint4 pk;
+                        pk.x = pack_half2(f[8 * q + 0], f[8 * q + 1]);
+                        pk.y = pack_half2(f[8 * q + 2], f[8 * q + 3]);
+                        pk.z = pack_half2(f[8 * q + 4], f[8 * q + 5]);
+                        pk.w = pack_half2(f[8 * q + 6], f[8 * q + 7]);
+                        reinterpret_cast<uint4*>(yrow)[q] = pk;
+                    }
+                    if (a.y32) {
+                        float* y32row = a.y32 + size_t(m) * a.N + nb;
 #pragma unroll
-                for (int q = 0; q < 8; ++q)
-                    reinterpret_cast<float4*>(y32row)[q] =
-                        make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
-            }
-        } else {
+                        for (int q = 0; q < 8; ++q)
+                            reinterpret_cast<float4*>(y32row)[q] =
+                                make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
+                    }
+                } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                if (nb + j < a.N) {
-                    yrow[j] = __half_as_ushort(__float2half_rn(f[j]));
-                    if (a.y32) a.y32[size_t(m) * a.N + nb + j] = f[j];
+                    for (int j = 0; j < 32; ++j) {
+                        if (nb + j < a.N) {
+                            yrow[j] = __half_as_ushort(__float2half_rn(f[j]));
+                            if (a.y32) a.y32[size_t(m) * a.N + nb + j] = f[j];
+                        }
+                    }
                 }
             }
+            // this accumulator may be overwritten by the MMAs of tile i + 2
+            asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc]));
         }
     }
 
@@ -296,8 +349,17 @@ cudaError_t launch_gemm_f16(const uint16_t* x, const uint16_t* w16, int64_t M, i
         if (e != cudaSuccess) return e;
         configured.fetch_or(bit);
     }
+    static std::atomic<int> sm_count[64];
+    int sms = sm_count[dev & 63].load(std::memory_order_relaxed);
+    if (sms == 0) {
+        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        sm_count[dev & 63].store(sms, std::memory_order_relaxed);
+    }
     GemmArgs a{bias, y, y32, int(M), N, K};
-    dim3 grid(unsigned((N + BN - 1) / BN), unsigned((M + BM - 1) / BM));
+    const int64_t tiles = ((M + BM - 1) / BM) * int64_t((N + BN - 1) / BN);
+    if (tiles > INT32_MAX) return cudaErrorInvalidValue;
+    const unsigned grid = unsigned(tiles < sms ? tiles : sms);  // persistent: one CTA per SM
     gemm_f16_kernel<<<grid, kGemmThreads, smem, s>>>(tx, tw, a);
     return cudaGetLastError();
 }

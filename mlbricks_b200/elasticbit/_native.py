@@ -359,33 +359,35 @@ class RuntimeMatrix:
     # -- execution -----------------------------------------------------------
     def _launch(self, x: torch.Tensor, M: int, bias: torch.Tensor | None, y: torch.Tensor,
                 y32: torch.Tensor | None) -> None:
+        # libebx selects the matrix's device itself; the stream is that device's current one
         ws_bytes = int(_LIB.ebx_linear_workspace_bytes(self._h, M))
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=self._cuda) if ws_bytes else None
         _ebx.check(_LIB.ebx_linear(
             self._h, x.data_ptr(), M, None if bias is None else bias.data_ptr(), y.data_ptr(),
             None if y32 is None else y32.data_ptr(), None if ws is None else ws.data_ptr(),
-            ws_bytes, _stream()))
+            ws_bytes, _ebx.stream_ptr(device=self._device)))
 
     def linear(self, x: torch.Tensor, bias: torch.Tensor | None = None,
                out32: bool = False) -> torch.Tensor | tuple[torch.Tensor, torch.Tensor]:
         """y = x @ W^T (+ bias) for any number of rows; x fp16 CUDA [..., cols]."""
-        if not x.is_cuda or x.dtype != torch.float16:
+        if x.dtype != torch.float16 or not x.is_cuda:
             raise ValueError("linear requires FP16 CUDA activations")
         if x.shape[-1] != self._cols:
             raise ValueError(f"expected last dimension {self._cols}, got {x.shape[-1]}")
         if x.get_device() != self._device:
             raise ValueError("input CUDA device does not match RuntimeMatrix device")
-        xc = x.contiguous()
+        xc = x if x.is_contiguous() else x.contiguous()
         M = xc.numel() // self._cols
         y = torch.empty((*x.shape[:-1], self._rows), dtype=torch.float16, device=x.device)
         y32 = torch.empty(y.shape, dtype=torch.float32, device=x.device) if out32 else None
         b = None
         if bias is not None:
-            b = bias.detach().to(device=x.device, dtype=torch.float16).contiguous()
+            b = bias.detach()
+            if b.dtype != torch.float16 or b.device != x.device or not b.is_contiguous():
+                b = b.to(device=x.device, dtype=torch.float16).contiguous()
             if b.numel() != self._rows:
                 raise ValueError("bias must match output features")
-        with torch.cuda.device(self._device):
-            self._launch(xc, M, b, y, y32)
+        self._launch(xc, M, b, y, y32)
         return (y, y32) if out32 else y
 
     def linear_allreduce(self, x: torch.Tensor, exchange, bias: torch.Tensor | None = None,
@@ -396,7 +398,9 @@ class RuntimeMatrix:
             raise ValueError("linear_allreduce requires FP16 CUDA activations")
         if x.shape[-1] != self._cols:
             raise ValueError(f"expected last dimension {self._cols}, got {x.shape[-1]}")
-        xc = x.contiguous()
+        if x.get_device() != self._device:
+            raise ValueError("input CUDA device does not match RuntimeMatrix device")
+        xc = x if x.is_contiguous() else x.contiguous()
         M = xc.numel() // self._cols
         y = torch.empty((*x.shape[:-1], self._rows), dtype=torch.float16, device=x.device)
         y32 = torch.empty(y.shape, dtype=torch.float32, device=x.device) if out32 else None
@@ -405,10 +409,10 @@ class RuntimeMatrix:
             b = bias.detach().to(device=x.device, dtype=torch.float16).contiguous()
             if b.numel() != self._rows:
                 raise ValueError("bias must match output features")
-        with torch.cuda.device(self._device):
-            _ebx.check(_LIB.ebx_linear_allreduce(
-                self._h, xc.data_ptr(), M, None if b is None else b.data_ptr(), y.data_ptr(),
-                None if y32 is None else y32.data_ptr(), exchange.handle, _stream()))
+        _ebx.check(_LIB.ebx_linear_allreduce(
+            self._h, xc.data_ptr(), M, None if b is None else b.data_ptr(), y.data_ptr(),
+            None if y32 is None else y32.data_ptr(), exchange.handle,
+            _ebx.stream_ptr(device=self._device)))
         return (y, y32) if out32 else y
 
     def forwardTorch(self, input: torch.Tensor) -> torch.Tensor:
