@@ -33,19 +33,27 @@ namespace ebx {
 namespace {
 
 constexpr int BM = 128;
-constexpr int BN = 256;
 constexpr int BK = 64;
-constexpr int kStagesG = 4;
 constexpr int kABytes = BM * BK * 2;
-constexpr int kBBytes = BN * BK * 2;
-constexpr int kStageBytesG = kABytes + kBBytes;
-constexpr int kAccCols = BN;             // one fp32 accumulator: 128 lanes x 256 columns
-constexpr int kTmemCols = 2 * kAccCols;  // double-buffered
 constexpr int kGemmThreads = 192;        // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr int kGroupM = 8;               // token tiles per raster group
 
-// instruction descriptor: D fp32, A/B fp16, both K-major, N = 256, M = 128
-constexpr uint32_t kIdesc = (1u << 4) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+// Per weight-tile width BN (256, 128 or 64 rows): the ring, the TMEM
+// accumulators (two of BN fp32 columns) and the MMA instruction descriptor
+// (D fp32, A/B fp16, both K-major, M = 128, N = BN).
+template <int BN>
+struct GemmCfg {
+    static constexpr int kBBytes = BN * BK * 2;
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kStages = 4 * (kABytes + 256 * BK * 2) / kStageBytes < 8
+                                       ? 4 * (kABytes + 256 * BK * 2) / kStageBytes
+                                       : 8;  // same ring bytes as BN = 256, at most 8 stages
+    static constexpr int kAccCols = BN;
+    static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+    static constexpr uint32_t kIdesc =
+        (1u << 4) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+    static constexpr int kSmem = kStages * kStageBytes + 1024 + 256;
+};
 
 __device__ int g_gemm_status = 0;
 
@@ -83,12 +91,12 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
 }
 
 __device__ __forceinline__ void umma_f16(uint32_t tmem, uint64_t adesc, uint64_t bdesc,
-                                         uint32_t accumulate) {
+                                         uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem),
-        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
@@ -109,9 +117,15 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
     nt = idx / gm;
 }
 
+template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_f16_kernel(const __grid_constant__ CUtensorMap tma_x, const __grid_constant__ CUtensorMap tma_w,
                     GemmArgs a) {
+    using G = GemmCfg<BN>;
+    constexpr int kStagesG = G::kStages;
+    constexpr int kStageBytesG = G::kStageBytes;
+    constexpr int kAccCols = G::kAccCols;
+    constexpr int kTmemCols = G::kTmemCols;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
@@ -195,7 +209,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     const uint32_t bbase = abase + kABytes;
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k)
-                        umma_f16(d, sw128_desc(abase + k * 32), sw128_desc(bbase + k * 32),
+                        umma_f16(d, sw128_desc(abase + k * 32), sw128_desc(bbase + k * 32), G::kIdesc,
                                  (kb | k) != 0 ? 1u : 0u);
                     umma_commit(smem_u32(&empty[st]));
                 }
@@ -332,23 +346,35 @@ bool gemm_supported(int K, const void* x, const void* w16) {
            (reinterpret_cast<uintptr_t>(w16) & 15) == 0 && encode_fn() != nullptr;
 }
 
-cudaError_t launch_gemm_f16(const uint16_t* x, const uint16_t* w16, int64_t M, int N, int K,
-                            const uint16_t* bias, uint16_t* y, float* y32, cudaStream_t s) {
-    if (M <= 0) return cudaSuccess;
+template <int BN>
+cudaError_t launch_gemm_bn(const uint16_t* x, const uint16_t* w16, int64_t M, int N, int K,
+                           const uint16_t* bias, uint16_t* y, float* y32, int sms, int dev,
+                           cudaStream_t s) {
+    using G = GemmCfg<BN>;
     CUtensorMap tx, tw;
-    if (!make_map(&tx, x, int(M), K, BM) || !make_map(&tw, w16, N, K, BN))
-        return cudaErrorInvalidValue;
-    constexpr int smem = kStagesG * kStageBytesG + 1024 + 256;
+    if (!make_map(&tx, x, int(M), K, BM) || !make_map(&tw, w16, N, K, BN)) return cudaErrorInvalidValue;
+    auto kern = gemm_f16_kernel<BN>;
     static std::atomic<uint64_t> configured{0};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
     const uint64_t bit = 1ull << (dev & 63);
     if (!(configured.load(std::memory_order_relaxed) & bit)) {
-        e = cudaFuncSetAttribute(gemm_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmem);
         if (e != cudaSuccess) return e;
         configured.fetch_or(bit);
     }
+    GemmArgs a{bias, y, y32, int(M), N, K};
+    const int64_t tiles = ((M + BM - 1) / BM) * int64_t((N + BN - 1) / BN);
+    if (tiles > INT32_MAX) return cudaErrorInvalidValue;
+    const unsigned grid = unsigned(tiles < sms ? tiles : sms);  // persistent: one CTA per SM
+    kern<<<grid, kGemmThreads, G::kSmem, s>>>(tx, tw, a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_f16(const uint16_t* x, const uint16_t* w16, int64_t M, int N, int K,
+                            const uint16_t* bias, uint16_t* y, float* y32, cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
     static std::atomic<int> sm_count[64];
     int sms = sm_count[dev & 63].load(std::memory_order_relaxed);
     if (sms == 0) {
@@ -356,12 +382,19 @@ cudaError_t launch_gemm_f16(const uint16_t* x, const uint16_t* w16, int64_t M, i
         if (e != cudaSuccess) return e;
         sm_count[dev & 63].store(sms, std::memory_order_relaxed);
     }
-    GemmArgs a{bias, y, y32, int(M), N, K};
-    const int64_t tiles = ((M + BM - 1) / BM) * int64_t((N + BN - 1) / BN);
-    if (tiles > INT32_MAX) return cudaErrorInvalidValue;
-    const unsigned grid = unsigned(tiles < sms ? tiles : sms);  // persistent: one CTA per SM
-    gemm_f16_kernel<<<grid, kGemmThreads, smem, s>>>(tx, tw, a);
-    return cudaGetLastError();
+    // Weight-tile width: estimated time = rounds of tiles over the SMs x tile width x a
+    // per-width cost factor (narrower tiles move more operand bytes per flop); small M
+    // takes narrow tiles so that M = 256 does not leave most of the GPU idle, while
+    // M = 1024 keeps one round of wide tiles rather than two rounds of narrow ones.
+    const int64_t m_tiles = (M + BM - 1) / BM;
+    auto cost = [&](int bn, int64_t factor_pct) {
+        const int64_t rounds = (m_tiles * ((N + bn - 1) / bn) + sms - 1) / sms;
+        return rounds * bn * factor_pct;
+    };
+    const int64_t c256 = cost(256, 100), c128 = cost(128, 115), c64 = cost(64, 135);
+    if (c256 <= c128 && c256 <= c64) return launch_gemm_bn<256>(x, w16, M, N, K, bias, y, y32, sms, dev, s);
+    if (c128 <= c64) return launch_gemm_bn<128>(x, w16, M, N, K, bias, y, y32, sms, dev, s);
+    return launch_gemm_bn<64>(x, w16, M, N, K, bias, y, y32, sms, dev, s);
 }
 
 }  // namespace ebx

@@ -320,8 +320,11 @@ def test_device_status_healthy_after_all_kernels(lib):
     assert st.value == 0
 
 
+# weight-tile widths chosen by the launcher's cost model: 64 for small grids (and the ragged
+# M = 2100 x N = 2600), 128 for M = 512 x N = 4096, 256 for M >= 1024 x N = 4096
 @pytest.mark.parametrize("M,rows,cols", [(65, 96, 512), (128, 256, 64), (300, 1000, 520),
-                                         (256, 1536, 384), (512, 4096, 4096), (200, 4096, 14336)])
+                                         (256, 1536, 384), (512, 4096, 4096), (200, 4096, 14336),
+                                         (1024, 4096, 512), (2048, 4096, 256), (2100, 2600, 200)])
 def test_prefill_gemm(lib, M, rows, cols):
     """M > 64: exact fp16 weight materialised into the workspace, tcgen05 GEMM."""
     bits = 10
