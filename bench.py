@@ -47,6 +47,11 @@ def algorithmic_bytes(N: int, K: int, bits: int, M: int) -> int:
     return math.ceil(N * K * bits / 8) + 4 * N + 2 * M * K + 2 * M * N
 
 
+# DRAM traffic of the decode kernel in one ncu capture (4096x14336, M = 1, 10-bit codes):
+# 73.49 MB read + 1.91 MB written for 73.47 MB of algorithmic bytes.
+DECODE_TRAFFIC_RATIO = (73.49 + 1.91) / 73.47
+
+
 def peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -304,8 +309,12 @@ def run_gpu(args) -> None:
         },
         "roofline": {
             "bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-            "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
-            "peak_source": pk["source"], "kernel": "ebx decode_kernel (M<=16)",
+            "frac": round(achieved / pk["hbm_gbs"], 4),
+            "traffic": round(step_bytes / nL * DECODE_TRAFFIC_RATIO),
+            "traffic_note": "bytes per launch: DRAM read+write / algorithmic bytes = "
+                            f"{DECODE_TRAFFIC_RATIO:.3f} in one ncu capture of the decode kernel "
+                            "(4096x14336, M=1), times this sweep's average algorithmic bytes per launch",
+            "peak_source": pk["source"], "kernel": "ebx decode_pipe_kernel (M<=16)",
         },
         "e2e": e2e,
         "prefill": prefill,
