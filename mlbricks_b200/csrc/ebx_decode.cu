@@ -277,11 +277,14 @@ __device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity) {
 // and empty (8 consumer-warp arrivals) mbarriers; every wait is bounded.
 constexpr int kMaxStages = 8;
 
-template <int B, int NT, int RG>
+// TPW: supertiles each consumer warp takes per round (one barrier wait, one
+// release and one loop trip per TPW tiles instead of per tile).
+template <int B, int NT, int RG, int TPW>
 struct PipeStage {
     static constexpr int kTileBytes = B * 128;
-    static constexpr int kWBytes = kWarps * kTileBytes;        // one row group's round
-    static constexpr int kXStride = kWarps * kKTile * 2 + 16;  // 1040 B: bank-shifted rows
+    static constexpr int kRound = kWarps * TPW;                // supertiles per round and row group
+    static constexpr int kWBytes = kRound * kTileBytes;        // one row group's round
+    static constexpr int kXStride = kRound * kKTile * 2 + 16;  // bank-shifted activation rows
     static constexpr int kRedBytes = RG * kWarps * NT * 128 * 4;
     // stage = RG weight rounds + activation rows of tokens 0..m-1 + one zero row
     static int bytes(int m) { return RG * kWBytes + (m + 1) * kXStride; }
@@ -292,9 +295,9 @@ struct PipeStage {
 // traffic per weight falls by RG.  Requires K % 64 == 0 (the generic kernel
 // covers the rest); activation rows of tokens >= M are zeroed once and never
 // written by the copy engine, so the fragment loads need no predicates.
-template <int B, bool HW, int NT, bool DIRECT, int RG, int MINB>
+template <int B, bool HW, int NT, bool DIRECT, int RG, int MINB, int TPW>
 __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(DecodeArgs a) {
-    using S = PipeStage<B, NT, RG>;
+    using S = PipeStage<B, NT, RG, TPW>;
     constexpr int kConsumers = kWarps * RG;
     extern __shared__ __align__(128) uint8_t smem[];
     const int D = a.stages;
@@ -304,7 +307,7 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
     float* red = reinterpret_cast<float*>(empty + kMaxStages);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int rounds = (a.kt + kWarps - 1) / kWarps;
+    const int rounds = (a.kt + S::kRound - 1) / S::kRound;
     const int mrows = a.M < NT * 8 ? a.M : NT * 8;
     const uint32_t xe = a.xa.world ? xchg_epoch(a.xa) + 1u : 0u;  // epoch this call publishes
 
@@ -331,7 +334,7 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
                 if (lane == 0) atomicExch(&g_device_status, kDeviceTimeout);
                 break;
             }
-            const int ntile = min(kWarps, a.kt - r * kWarps);
+            const int ntile = min(S::kRound, a.kt - r * S::kRound);
             const uint32_t xbytes = uint32_t(ntile * kKTile * 2);
             uint8_t* dst = smem + st * SB;
             const uint32_t bar = smem_u32(&full[st]);
@@ -345,14 +348,14 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
                     const int g = blockIdx.x * RG + rg;
                     if (g < a.groups)
                         bulk_g2s(smem_u32(dst + rg * S::kWBytes),
-                                 a.tiles + (size_t(g) * a.kt + size_t(r) * kWarps) * S::kTileBytes,
+                                 a.tiles + (size_t(g) * a.kt + size_t(r) * S::kRound) * S::kTileBytes,
                                  uint32_t(ntile * S::kTileBytes), bar);
                 }
             }
             __syncwarp();
             if (lane < mrows)
                 bulk_g2s(smem_u32(dst + RG * S::kWBytes + lane * S::kXStride),
-                         a.x + size_t(lane) * a.K + size_t(r) * kWarps * kKTile, xbytes, bar);
+                         a.x + size_t(lane) * a.K + size_t(r) * S::kRound * kKTile, xbytes, bar);
         }
     } else {
         // ---------------- consumer warps ----------------
@@ -392,7 +395,7 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
         for (int nb = 0; nb < NT; ++nb) {
             const int tok = r0 + 8 * nb;
             xrow[nb] = smem + RG * S::kWBytes + (tok < mrows ? tok : mrows) * S::kXStride +
-                       wt * kKTile * 2 + 32 * c;
+                       wt * TPW * kKTile * 2 + 32 * c;
         }
 
         int st = 0, ph = 0;
@@ -401,8 +404,10 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
                 if (lane == 0) atomicExch(&g_device_status, kDeviceTimeout);
                 break;
             }
-            const bool have = grp_ok && (r * kWarps + wt < a.kt);
-            const uint8_t* sw = smem + st * SB + rgl * S::kWBytes + wt * S::kTileBytes;
+#pragma unroll
+          for (int j = 0; j < TPW; ++j) {
+            const bool have = grp_ok && (r * S::kRound + wt * TPW + j < a.kt);
+            const uint8_t* sw = smem + st * SB + rgl * S::kWBytes + (wt * TPW + j) * S::kTileBytes;
             uint32_t w[B];
             uint32_t xb[NT][8];
             if (have) {
@@ -423,13 +428,16 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
                 for (int nb = 0; nb < NT; ++nb)
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
-                        const uint4 v = *reinterpret_cast<const uint4*>(xrow[nb] + st * SB + 16 * h);
+                        const uint4 v = *reinterpret_cast<const uint4*>(xrow[nb] + st * SB +
+                                                                        j * kKTile * 2 + 16 * h);
                         xb[nb][4 * h] = v.x; xb[nb][4 * h + 1] = v.y;
                         xb[nb][4 * h + 2] = v.z; xb[nb][4 * h + 3] = v.w;
                     }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&empty[st]));
+            if (j == TPW - 1) {  // every load of this stage has been issued
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&empty[st]));
+            }
             if (!have) continue;
 #pragma unroll
             for (int s = 0; s < 4; ++s) {
@@ -472,6 +480,7 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
                     mma_16816(acc[nb], af, xb[nb][(s >> 1) * 4 + (s & 1) * 2],
                               xb[nb][(s >> 1) * 4 + (s & 1) * 2 + 1]);
             }
+          }
         }
 #pragma unroll
         for (int nb = 0; nb < NT; ++nb)
@@ -571,9 +580,9 @@ cudaError_t launch_one(DecodeArgs& a, int groups, cudaStream_t s) {
     return launch_maybe_xchg(kern, a, unsigned(groups), kThreads, smem, s);
 }
 
-template <int B, bool HW, int NT, bool DIRECT, int RG>
+template <int B, bool HW, int NT, bool DIRECT, int RG, int TPW>
 cudaError_t launch_pipe(DecodeArgs& a, int groups, cudaStream_t s) {
-    using S = PipeStage<B, NT, RG>;
+    using S = PipeStage<B, NT, RG, TPW>;
     // RG == 1: three CTAs per SM (27 warps); RG == 2: one CTA per SM.  The ring
     // is as deep as that budget allows for this M (2..kMaxStages stages).
     constexpr int MINB = RG == 1 ? 3 : 1;
@@ -582,10 +591,11 @@ cudaError_t launch_pipe(DecodeArgs& a, int groups, cudaStream_t s) {
     const int mrows = a.M < NT * 8 ? a.M : NT * 8;
     a.stage_bytes = S::bytes(mrows);
     int D = (kBudget - kFixed) / a.stage_bytes;
-    D = D > kMaxStages ? kMaxStages : (D < 2 ? 2 : D);
+    D = D > kMaxStages ? kMaxStages : D;
+    if (D < 2) return cudaErrorInvalidConfiguration;  // dispatch keeps every case >= 2 stages
     a.stages = D;
     const int smem = D * a.stage_bytes + kFixed;
-    auto kern = decode_pipe_kernel<B, HW, NT, DIRECT, RG, MINB>;
+    auto kern = decode_pipe_kernel<B, HW, NT, DIRECT, RG, MINB, TPW>;
     static std::atomic<uint64_t> configured{0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -602,15 +612,23 @@ cudaError_t launch_pipe(DecodeArgs& a, int groups, cudaStream_t s) {
 template <int B, bool HW>
 cudaError_t dispatch_nt(DecodeArgs& a, int groups, bool pipe, bool direct, cudaStream_t s) {
     if (pipe) {
+        // M <= 4 and b <= 12: two supertiles per warp per round (a stage of 16 supertiles
+        // and up to 5 activation rows still leaves >= 2 stages in the 74 KB budget);
+        // M <= 8: one per warp; M <= 16: two row groups per CTA share each activation slice.
         constexpr bool kCanDirect = !HW && B != kFp16Bits;
+        if (B <= 12 && a.M <= 4) {
+            if constexpr (kCanDirect)
+                if (direct) return launch_pipe<B, HW, 1, true, 1, 2>(a, groups, s);
+            return launch_pipe<B, HW, 1, false, 1, 2>(a, groups, s);
+        }
         if (a.M <= 8) {
             if constexpr (kCanDirect)
-                if (direct) return launch_pipe<B, HW, 1, true, 1>(a, groups, s);
-            return launch_pipe<B, HW, 1, false, 1>(a, groups, s);
+                if (direct) return launch_pipe<B, HW, 1, true, 1, 1>(a, groups, s);
+            return launch_pipe<B, HW, 1, false, 1, 1>(a, groups, s);
         }
         if constexpr (kCanDirect)
-            if (direct) return launch_pipe<B, HW, 2, true, 2>(a, groups, s);
-        return launch_pipe<B, HW, 2, false, 2>(a, groups, s);
+            if (direct) return launch_pipe<B, HW, 2, true, 2, 1>(a, groups, s);
+        return launch_pipe<B, HW, 2, false, 2, 1>(a, groups, s);
     }
     return a.M <= 8 ? launch_one<B, HW, 1, false>(a, groups, s) : launch_one<B, HW, 2, false>(a, groups, s);
 }
