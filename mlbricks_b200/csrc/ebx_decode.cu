@@ -614,7 +614,9 @@ cudaError_t dispatch_nt(DecodeArgs& a, int groups, bool pipe, bool direct, cudaS
     if (pipe) {
         // M <= 4 and b <= 12: two supertiles per warp per round (a stage of 16 supertiles
         // and up to 5 activation rows still leaves >= 2 stages in the 74 KB budget);
-        // M <= 8: one per warp; M <= 16: two row groups per CTA share each activation slice.
+        // M <= 8: one per warp; M <= 16: one row group per CTA with 16 activation rows
+        // (two stages; measured faster than two row groups per CTA at one CTA per SM,
+        // whose 448-CTA grid for N = 14336 runs in 3.03 waves).
         constexpr bool kCanDirect = !HW && B != kFp16Bits;
         if (B <= 12 && a.M <= 4) {
             if constexpr (kCanDirect)
@@ -626,9 +628,11 @@ cudaError_t dispatch_nt(DecodeArgs& a, int groups, bool pipe, bool direct, cudaS
                 if (direct) return launch_pipe<B, HW, 1, true, 1, 1>(a, groups, s);
             return launch_pipe<B, HW, 1, false, 1, 1>(a, groups, s);
         }
+        if constexpr (B == kFp16Bits)  // 16-bit weights: two stages need the larger budget
+            return launch_pipe<B, HW, 2, false, 2, 1>(a, groups, s);
         if constexpr (kCanDirect)
-            if (direct) return launch_pipe<B, HW, 2, true, 2, 1>(a, groups, s);
-        return launch_pipe<B, HW, 2, false, 2, 1>(a, groups, s);
+            if (direct) return launch_pipe<B, HW, 2, true, 1, 1>(a, groups, s);
+        return launch_pipe<B, HW, 2, false, 1, 1>(a, groups, s);
     }
     return a.M <= 8 ? launch_one<B, HW, 1, false>(a, groups, s) : launch_one<B, HW, 2, false>(a, groups, s);
 }
