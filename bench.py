@@ -382,8 +382,8 @@ def build_stack(device, world: int, rank: int, collectives, exchange=None):
             del w
             if fuse_gate_up and name in ("gate", "up"):
                 pending[name] = (q, sc)
-                if len(pending) == 2:  # one launch for both: [gate rows | up rows] of this rank
-                    layer["gate_up"] = tp.build_column_fused([pending["gate"], pending["up"]],
+                if len(pending) == 2:  # one launch: gate/up interleaved, SwiGLU in the epilogue
+                    layer["swiglu"] = tp.build_column_swiglu(pending["gate"], pending["up"],
                                                              bits_of["gate"], world, rank)
                     pending.clear()
                 continue
@@ -411,12 +411,10 @@ def stack_step(layers, head, h, world: int):
         qkv = L["qkv"](h)                               # [M, 6144 / W] local
         attn = qkv[:, : 4096 // world]                  # local heads -> O's K slice
         h = L["o"](attn)                                # all-reduce -> [M, 4096]
-        if "gate_up" in L:
-            gu = L["gate_up"](h)                        # [M, 2 * 14336 / W] local
-            g, u = gu.split(L["gate_up"].part_widths, dim=-1)
+        if "swiglu" in L:
+            act = L["swiglu"](h)                        # [M, 14336 / W] local, fp16
         else:
-            g, u = L["gate"](h), L["up"](h)
-        act = torch.nn.functional.silu(g) * u           # fp16
+            act = torch.nn.functional.silu(L["gate"](h)) * L["up"](h)
         h = L["down"](act)                              # all-reduce -> [M, 4096]
     return head(h)
 
@@ -438,7 +436,8 @@ def run_tp_stack(args, world: int, rank: int, device) -> dict:
                        f"Megatron TP over {world} GPU(s); row-parallel all-reduce: "
                        + ("libebx exchange (M<=16), NCCL fp32 (M>16)" if exchange else
                           "NCCL fp32" if world > 1 else "none") +
-                       "; gate/up fused per rank; one CUDA graph per decode step",
+                       "; gate/up interleaved per rank with SwiGLU fused into the decode epilogue (M<=16); "
+                       "one CUDA graph per decode step",
            "bits": bits_of, "decode_tok_s": {}}
     stream = torch.cuda.Stream(device)
     for M in (1, 16, 64):

@@ -188,6 +188,17 @@ EBX_API ebx_status ebx_elastic_linear_packed(const void* x, int32_t x_dtype, int
                                      int64_t group_size, int64_t out_features,
                                      int64_t in_features, void* out, void* stream);
 
+/* SwiGLU projection for decode batches: m holds a gate and an up projection
+ * with their rows interleaved in blocks of 8 (rows 16j..16j+7 = gate rows
+ * 8j..8j+7, rows 16j+8..16j+15 = up rows 8j..8j+7; rows % 16 == 0), and
+ * y[M, rows/2] = fp16( silu(g) * u ) with g, u the fp32 sums x @ W^T (+ bias,
+ * in the same interleaved order, may be NULL) before any rounding.  One launch
+ * replaces "gate/up GEMV, silu, multiply".  1 <= M <= 16; y32 (fp32 copy, may be
+ * NULL).  No reference counterpart (the reference computes gate and up as two
+ * linears and the activation in PyTorch). */
+EBX_API ebx_status ebx_linear_swiglu(const ebx_matrix* m, const void* x, int64_t M, const void* bias,
+                                     void* y, float* y32, void* stream);
+
 /* ---- Tensor-parallel exchange (row-parallel linear + all-reduce) ----------
  * No reference counterpart: the reference has no distributed code.  These
  * replace "row-parallel shard GEMV, then an NCCL all-reduce of the fp32

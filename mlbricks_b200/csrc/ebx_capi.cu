@@ -388,6 +388,28 @@ ebx_status ebx_linear(const ebx_matrix* h, const void* x, int64_t M, const void*
     return EBX_OK;
 }
 
+ebx_status ebx_linear_swiglu(const ebx_matrix* h, const void* x, int64_t M, const void* bias,
+                             void* y, float* y32, void* stream) {
+    if (!h || (M > 0 && (!x || !y))) {
+        set_error("null argument");
+        return EBX_ERR_INVALID;
+    }
+    if (M < 0 || M > 16) {
+        set_error("ebx_linear_swiglu: need 0 <= M <= 16 (decode batches)");
+        return EBX_ERR_INVALID;
+    }
+    if (h->m.rows % 16 != 0) {
+        set_error("ebx_linear_swiglu: rows must be a multiple of 16 (gate/up interleaved by 8)");
+        return EBX_ERR_INVALID;
+    }
+    if (M == 0) return EBX_OK;
+    DeviceGuard g(h->m.device);
+    EBX_CUDA(ebx::launch_decode(h->m, static_cast<const uint16_t*>(x), M,
+                                static_cast<const uint16_t*>(bias), static_cast<uint16_t*>(y), y32,
+                                static_cast<cudaStream_t>(stream), nullptr, 1));
+    return EBX_OK;
+}
+
 ebx_status ebx_device_status(int32_t device, int32_t* status, int32_t clear) {
     if (!status) {
         set_error("null argument");

@@ -52,7 +52,34 @@ struct DecodeArgs {
     int stages;       // pipe kernel: ring depth (runtime, <= kMaxStages)
     int stage_bytes;  // pipe kernel: RG weight rounds + (min(M, 8 NT) + 1) activation rows
     XchgArgs xa;      // world > 0: fp32 partials go to the tensor-parallel exchange
+    int act;          // 1: SwiGLU over interleaved gate/up rows (y has N / 2 columns)
 };
+
+// SwiGLU epilogue.  The matrix holds gate and up rows interleaved in blocks of 8
+// (rows 16j..16j+7 = gate rows 8j..8j+7, rows 16j+8..16j+15 = the matching up
+// rows), so the two sums of one output sit in fragment elements i and i + 2 of
+// the same lane: y[tok, 8j + r] = fp16(silu(g) * u) from the fp32 sums (bias, if
+// any, added to each first; integer-path scales applied per row).
+template <int B, bool HW>
+__device__ __forceinline__ void store_swiglu(const DecodeArgs& a, int g, int l, int tok, float vg,
+                                             float vu) {
+    const int grow = g * kRowGroup + (l >> 2);
+    const int urow = grow + 8;
+    if (urow >= a.N || tok >= a.M) return;
+    if constexpr (HW && B != kFp16Bits) {
+        vg *= a.scales[grow];
+        vu *= a.scales[urow];
+    }
+    if (a.bias) {
+        vg += __half2float(__ushort_as_half(a.bias[grow]));
+        vu += __half2float(__ushort_as_half(a.bias[urow]));
+    }
+    const float v = vg / (1.0f + __expf(-vg)) * vu;
+    const int nout = a.N >> 1;
+    const int col = g * 8 + (l >> 2);
+    a.y[size_t(tok) * nout + col] = __half_as_ushort(__float2half_rn(v));
+    if (a.y32) a.y32[size_t(tok) * nout + col] = v;
+}
 
 // Fused exchange: all ranks' partials of (tok, row) -> bias -> one fp16 rounding.
 __device__ __forceinline__ void xchg_finish_one(const DecodeArgs& a, uint32_t e, int tok, int row) {
@@ -228,6 +255,15 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         for (int ww = 0; ww < kWarps; ++ww) v += red[((ww * NT + nb) * 32 + l) * 4 + i];
         const int row = g * kRowGroup + (l >> 2) + 8 * (i >> 1);
         const int tok = 8 * nb + (l & 3) * 2 + (i & 1);
+        if (a.act) {
+            if ((i >> 1) == 0) {
+                float vu = 0.0f;
+#pragma unroll
+                for (int ww = 0; ww < kWarps; ++ww) vu += red[((ww * NT + nb) * 32 + l) * 4 + i + 2];
+                store_swiglu<B, HW>(a, g, l, tok, v, vu);
+            }
+            continue;
+        }
         if (row < a.N && tok < a.M) {
             if constexpr (HW && B != kFp16Bits) v = v * a.scales[row];
             if (a.xa.world) {
@@ -499,6 +535,16 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
         for (int ww = 0; ww < kWarps; ++ww) v += red[(((rgl * kWarps + ww) * NT + nb) * 32 + l) * 4 + i];
         const int row = g * kRowGroup + (l >> 2) + 8 * (i >> 1);
         const int tok = 8 * nb + (l & 3) * 2 + (i & 1);
+        if (a.act) {
+            if ((i >> 1) == 0 && g < a.groups) {
+                float vu = 0.0f;
+#pragma unroll
+                for (int ww = 0; ww < kWarps; ++ww)
+                    vu += red[(((rgl * kWarps + ww) * NT + nb) * 32 + l) * 4 + i + 2];
+                store_swiglu<B, HW>(a, g, l, tok, v, vu);
+            }
+            continue;
+        }
         if (g < a.groups && row < a.N && tok < a.M) {
             if constexpr (HW && B != kFp16Bits) v = v * a.scales[row];
             if (a.xa.world) {
@@ -652,8 +698,9 @@ cudaError_t read_device_status(int* status, bool clear, cudaStream_t s) {
 }
 
 cudaError_t launch_decode(const Matrix& m, const uint16_t* x, int64_t M, const uint16_t* bias,
-                          uint16_t* y, float* y32, cudaStream_t s, XchgArgs* xa) {
+                          uint16_t* y, float* y32, cudaStream_t s, XchgArgs* xa, int act) {
     if (M <= 0) return cudaSuccess;
+    if (act && (xa || (m.rows % 16) != 0)) return cudaErrorInvalidValue;
     if (xa && M > 16) return cudaErrorInvalidValue;  // one launch = one exchange epoch
     const bool vecx = (m.cols % 64) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
     const bool hw = m.exec_width < 16 && m.bits <= 8;
@@ -663,8 +710,10 @@ cudaError_t launch_decode(const Matrix& m, const uint16_t* x, int64_t M, const u
         a.scales = m.scales;
         a.x = x + m0 * m.cols;
         a.bias = bias;
-        a.y = y ? y + m0 * m.rows : nullptr;
-        a.y32 = y32 ? y32 + m0 * m.rows : nullptr;
+        const int64_t ycols = act ? m.rows / 2 : m.rows;
+        a.y = y ? y + m0 * ycols : nullptr;
+        a.y32 = y32 ? y32 + m0 * ycols : nullptr;
+        a.act = act;
         if (xa) a.xa = *xa;
         a.M = int(M - m0 < 16 ? M - m0 : 16);
         a.N = m.rows;

@@ -64,8 +64,10 @@ struct XchgArgs {
 // co-resident it is launched cooperatively with xa->fused = 1 and also waits
 // for all ranks' partials of its own outputs, reduces them, writes y / y32 and
 // advances the epoch; otherwise xa->fused = 0 and launch_xchg_finish must follow.
+// act = 1: SwiGLU over gate/up rows interleaved in blocks of 8 (y has rows / 2 columns).
 cudaError_t launch_decode(const Matrix& m, const uint16_t* x, int64_t M, const uint16_t* bias,
-                          uint16_t* y, float* y32, cudaStream_t s, XchgArgs* xa = nullptr);
+                          uint16_t* y, float* y32, cudaStream_t s, XchgArgs* xa = nullptr,
+                          int act = 0);
 // Reads (and optionally clears) the device-side status word that bounded
 // waits set on timeout (0 = healthy).  Synchronizes `s`.
 cudaError_t read_device_status(int* status, bool clear, cudaStream_t s);

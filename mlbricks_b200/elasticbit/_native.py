@@ -390,6 +390,30 @@ class RuntimeMatrix:
         self._launch(xc, M, b, y, y32)
         return (y, y32) if out32 else y
 
+    def linear_swiglu(self, x: torch.Tensor, bias: torch.Tensor | None = None,
+                      out32: bool = False):
+        """fp16(silu(g) * u) for a matrix whose gate/up rows are interleaved in blocks of 8
+        (ebx_linear_swiglu); x fp16 CUDA [..., cols] with at most 16 rows."""
+        if x.dtype != torch.float16 or not x.is_cuda:
+            raise ValueError("linear_swiglu requires FP16 CUDA activations")
+        if x.shape[-1] != self._cols:
+            raise ValueError(f"expected last dimension {self._cols}, got {x.shape[-1]}")
+        if x.get_device() != self._device:
+            raise ValueError("input CUDA device does not match RuntimeMatrix device")
+        xc = x if x.is_contiguous() else x.contiguous()
+        M = xc.numel() // self._cols
+        y = torch.empty((*x.shape[:-1], self._rows // 2), dtype=torch.float16, device=x.device)
+        y32 = torch.empty(y.shape, dtype=torch.float32, device=x.device) if out32 else None
+        b = None
+        if bias is not None:
+            b = bias.detach().to(device=x.device, dtype=torch.float16).contiguous()
+            if b.numel() != self._rows:
+                raise ValueError("bias must match the interleaved rows")
+        _ebx.check(_LIB.ebx_linear_swiglu(
+            self._h, xc.data_ptr(), M, None if b is None else b.data_ptr(), y.data_ptr(),
+            None if y32 is None else y32.data_ptr(), _ebx.stream_ptr(device=self._device)))
+        return (y, y32) if out32 else y
+
     def linear_allreduce(self, x: torch.Tensor, exchange, bias: torch.Tensor | None = None,
                          out32: bool = False):
         """Row-parallel shard + all-reduce in one libebx call (ebx_linear_allreduce):

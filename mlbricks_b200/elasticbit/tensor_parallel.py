@@ -264,5 +264,62 @@ def build_column_fused(parts, bits: int, world: int, rank: int, *, threshold: fl
     return lin
 
 
+def interleave_by8(gate, up):
+    """Rows of `gate` and `up` ([I, ...] each, I % 8 == 0) interleaved in blocks of 8:
+    rows 16j..16j+7 = gate rows 8j..8j+7, rows 16j+8..16j+15 = up rows 8j..8j+7
+    (the layout ebx_linear_swiglu reads).  numpy arrays or torch tensors."""
+    n = int(gate.shape[0])
+    if n % 8 or int(up.shape[0]) != n:
+        raise ValueError("gate and up need the same row count, a multiple of 8")
+    rest = tuple(gate.shape[1:])
+    if torch.is_tensor(gate):
+        return torch.stack([gate.reshape(n // 8, 8, *rest), up.reshape(n // 8, 8, *rest)], 1) \
+            .reshape(2 * n, *rest).contiguous()
+    g = np.asarray(gate).reshape(n // 8, 8, *rest)
+    u = np.asarray(up).reshape(n // 8, 8, *rest)
+    return np.ascontiguousarray(np.stack([g, u], 1).reshape(2 * n, *rest))
+
+
+class SwiGLULinear(torch.nn.Module):
+    """One rank's column-parallel gate/up pair with the SwiGLU activation fused:
+    forward(x) = silu(x @ Wg_r^T) * (x @ Wu_r^T) over this rank's slice of the
+    intermediate dimension.  Decode batches (<= 16 rows) run ebx_linear_swiglu (one
+    launch, activation from the fp32 sums); larger batches run ebx_linear on the
+    interleaved matrix and the activation in torch."""
+
+    def __init__(self, matrix, width: int, in_features: int) -> None:
+        super().__init__()
+        self.matrix = matrix
+        self.width = int(width)
+        self.in_features = int(in_features)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        native = getattr(self.matrix, "_native", self.matrix)
+        if x.numel() // x.shape[-1] <= 16:
+            return native.linear_swiglu(x)
+        y = native.linear(x).view(*x.shape[:-1], self.width // 8, 2, 8)
+        return (torch.nn.functional.silu(y[..., 0, :]) * y[..., 1, :]).reshape(*x.shape[:-1],
+                                                                               self.width)
+
+
+def build_column_swiglu(gate, up, bits: int, world: int, rank: int, *, threshold: float = 0.0,
+                        error: float = 0.0, decodePolicy: str = "fullPrecision") -> SwiGLULinear:
+    """This rank's column slice of a gate/up pair (global codes and scales each, same
+    width) as one interleaved matrix with the SwiGLU activation fused."""
+    from .core import RuntimeMatrix
+
+    (gc, gs), (uc, us) = gate, up
+    K = int(gc.shape[1])
+    cg, sg, (lo, hi) = shard_codes(gc, gs, "column", world, rank)
+    cu, su, _ = shard_codes(uc, us, "column", world, rank)
+    width = hi - lo
+    c = interleave_by8(cg, cu)
+    s = interleave_by8(sg if torch.is_tensor(sg) else np.asarray(sg),
+                       su if torch.is_tensor(su) else np.asarray(su))
+    m = RuntimeMatrix._compressSelectedCodes(c, s, bits, threshold, error, decodePolicy=decodePolicy)
+    return SwiGLULinear(m, width, K)
+
+
 __all__ = ["MODES", "shard_bounds", "shard_codes", "Collectives", "Exchange", "ShardedLinear",
-           "build_sharded", "build_column_fused"]
+           "build_sharded", "build_column_fused", "interleave_by8", "SwiGLULinear",
+           "build_column_swiglu"]

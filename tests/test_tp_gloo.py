@@ -103,3 +103,42 @@ def test_row_and_column_parallel_match_unsharded_on_gloo():
             rel = np.linalg.norm(y - ref) / np.linalg.norm(ref)
             assert rel < 1e-3, (mode, rel)
             assert np.abs(y - ref).max() <= max(2e-3, float(np.abs(np.spacing(ref.astype(np.float16))).max()))
+
+
+def test_interleave_by8_layout_numpy_and_torch():
+    from mlbricks_b200.elasticbit.tensor_parallel import interleave_by8
+
+    g = np.arange(16 * 3).reshape(16, 3)
+    u = -np.arange(16 * 3).reshape(16, 3)
+    out = interleave_by8(g, u)
+    assert out.shape == (32, 3)
+    assert np.array_equal(out[0:8], g[0:8]) and np.array_equal(out[8:16], u[0:8])
+    assert np.array_equal(out[16:24], g[8:16]) and np.array_equal(out[24:32], u[8:16])
+    tout = interleave_by8(torch.from_numpy(g), torch.from_numpy(u))
+    assert np.array_equal(tout.numpy(), out)
+    s = interleave_by8(np.arange(8.0), np.arange(8.0) + 100)
+    assert np.array_equal(s, np.concatenate([np.arange(8.0), np.arange(8.0) + 100]))
+    with pytest.raises(ValueError):
+        interleave_by8(np.zeros((12, 2)), np.zeros((12, 2)))
+
+
+def test_swiglu_module_large_batch_deinterleaves():
+    """M > 16 path: ebx_linear on the interleaved matrix, activation in torch."""
+    from mlbricks_b200.elasticbit.tensor_parallel import SwiGLULinear, interleave_by8
+
+    rng = np.random.default_rng(0)
+    I, K, M = 24, 10, 20
+    wg = rng.standard_normal((I, K)).astype(np.float32)
+    wu = rng.standard_normal((I, K)).astype(np.float32)
+    w = torch.from_numpy(interleave_by8(wg, wu))
+
+    class Stand:
+        def linear(self, x):
+            return x @ w.T
+
+    mod = SwiGLULinear(Stand(), I, K)
+    x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32))
+    y = mod(x)
+    g = x @ torch.from_numpy(wg).T
+    u = x @ torch.from_numpy(wu).T
+    assert torch.allclose(y, torch.nn.functional.silu(g) * u, atol=1e-5)
