@@ -394,4 +394,108 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
 }
 
+// ---------------------------------------------------------------------------
+// Paired exact dequantisation (b = 8..12, fullPrecision semantics)
+// ---------------------------------------------------------------------------
+// A lane's codes j and j + 16 feed the same row (fragment element e = j mod 8).
+// Each code is read from a "view" of the lane's word string: its own word, or a
+// funnel shift of its word pair, placed so that the code sits at an offset o
+// with o + b <= 23 and so that codes j and j + 16 sit at the same o:
+//   b <= 11: views start at codes 0, 2, 4, ...; code j at o = (j & 1) * b, so
+//            one shift serves two codes;
+//   b = 12:  a code at bit 0, 4 or 8 of its word is used in place, any other
+//            code is shifted to bit 0 (16 * 12 is a multiple of 32, so codes j
+//            and j + 16 have the same position within their words).
+// With the float of exponent 23 - o, (view & mask << o) | exponent is exactly
+// 2^(23-o) + code.  One f32x2 add of -(2^(23-o) + qmax) gives both codes' q
+// exactly; one f32x2 RN multiply by (s, s) gives fp32_rn(q * s) for both, the
+// reference's static_cast<float>(q) * scale; cvt.rn.f16x2 then rounds once to
+// fp16 as __float2half_rn does.
+template <int B>
+struct PairPlan {
+    static_assert(B >= 8 && B <= 12, "paired plan covers 8..12-bit codes");
+    static constexpr int kOffsets = B <= 11 ? 2 : 3;
+    static constexpr int off(int j) {
+        return B <= 11 ? (j & 1) * B : (((j * B) & 31) + B <= 23 ? ((j * B) & 31) : 0);
+    }
+    static constexpr int view(int j) { return j * B - off(j); }  // first bit of the view
+    static constexpr int off_index(int o) { return B <= 11 ? (o == 0 ? 0 : 1) : o / 4; }
+    static constexpr int offset_at(int i) { return B <= 11 ? i * B : i * 4; }
+};
+
+// The 32 bits of the lane's word string starting at bit V (zeros past the end).
+template <int B, int V>
+__device__ __forceinline__ uint32_t view_word(const uint32_t (&w)[B]) {
+    constexpr int wi = V >> 5, sh = V & 31;
+    if constexpr (sh == 0) return w[wi];
+    else if constexpr (wi + 1 >= B) return w[wi] >> sh;
+    else return __funnelshift_r(w[wi], w[wi + 1], sh);
+}
+
+// Constants of the paired decode, built once per thread: magic[i] is the float
+// 2^(23 - o_i) as bits, nbias[i] the pair (-(2^(23 - o_i) + qmax), same).
+template <int B>
+struct PairConsts {
+    uint32_t magic[3];
+    uint64_t nbias[3];
+    // magic23: the bits of 2^23 (0x4B000000), passed in at run time so that
+    // the compiler keeps the constants in registers
+    __device__ __forceinline__ void init(uint32_t magic23) {
+#pragma unroll
+        for (int i = 0; i < PairPlan<B>::kOffsets; ++i) {
+            const int o = PairPlan<B>::offset_at(i);
+            magic[i] = magic23 - (uint32_t(o) << 23);
+            const float nb = -(float(1u << (23 - o)) + float(qmax_for(B)));
+            nbias[i] = pack2f(nb, nb);
+        }
+    }
+};
+
+// fp32_rn(q * s) of codes J and J + 16 (scale pair s2 = (s, s) of their row).
+template <int B, int J>
+__device__ __forceinline__ void dequant_pair(const uint32_t (&w)[B], const PairConsts<B>& k,
+                                             uint64_t s2, float& lo, float& hi) {
+    using PP = PairPlan<B>;
+    constexpr int O = PP::off(J);
+    static_assert(PP::off(J + 16) == O, "paired codes share their in-view offset");
+    constexpr int I = PP::off_index(O);
+    constexpr uint32_t kMask = ((1u << B) - 1u) << O;
+    const uint32_t va = view_word<B, PP::view(J)>(w);
+    const uint32_t vb = view_word<B, PP::view(J + 16)>(w);
+    uint32_t ra, rb;
+    asm("{\n\t.reg .b32 c0, c1;\n\t.reg .b64 a;\n\t"
+        "lop3.b32 c0, %2, %4, %5, 0xEA;\n\t"
+        "lop3.b32 c1, %3, %4, %5, 0xEA;\n\t"
+        "mov.b64 a, {c0, c1};\n\t"
+        "add.rn.f32x2 a, a, %6;\n\t"
+        "mul.rn.f32x2 a, a, %7;\n\t"
+        "mov.b64 {%0, %1}, a;\n\t}"
+        : "=r"(ra), "=r"(rb)
+        : "r"(va), "r"(vb), "n"(kMask), "r"(k.magic[I]), "l"(k.nbias[I]), "l"(s2));
+    lo = __uint_as_float(ra);
+    hi = __uint_as_float(rb);
+}
+
+// A-fragments of k-steps S and S + 2 (codes 8S..8S+7 and 8S+16..8S+23):
+// register rr of a step holds codes 2rr, 2rr + 1 of that step (row r0 + 8 for rr odd).
+template <int B, int S>
+__device__ __forceinline__ void dequant_steps(const uint32_t (&w)[B], const PairConsts<B>& k,
+                                              const uint64_t (&s2)[2], uint32_t (&af_lo)[4],
+                                              uint32_t (&af_hi)[4]) {
+    float fl[8], fh[8];
+    dequant_pair<B, 8 * S + 0>(w, k, s2[0], fl[0], fh[0]);
+    dequant_pair<B, 8 * S + 1>(w, k, s2[0], fl[1], fh[1]);
+    dequant_pair<B, 8 * S + 2>(w, k, s2[1], fl[2], fh[2]);
+    dequant_pair<B, 8 * S + 3>(w, k, s2[1], fl[3], fh[3]);
+    dequant_pair<B, 8 * S + 4>(w, k, s2[0], fl[4], fh[4]);
+    dequant_pair<B, 8 * S + 5>(w, k, s2[0], fl[5], fh[5]);
+    dequant_pair<B, 8 * S + 6>(w, k, s2[1], fl[6], fh[6]);
+    dequant_pair<B, 8 * S + 7>(w, k, s2[1], fl[7], fh[7]);
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) {
+        af_lo[rr] = pack_half2(fl[2 * rr], fl[2 * rr + 1]);
+        af_hi[rr] = pack_half2(fh[2 * rr], fh[2 * rr + 1]);
+    }
+}
+
 }  // namespace ebx

@@ -23,6 +23,8 @@
 // Bias is added in fp32 before the single fp16 rounding, as cuBLAS does for
 // F.linear(x, W, b) on the reference's M>1 route.
 #include <atomic>
+#include <cstdlib>
+#include <cstring>
 
 #include "ebx_common.cuh"
 #include "ebx_internal.h"
@@ -53,6 +55,7 @@ struct DecodeArgs {
     int stage_bytes;  // pipe kernel: RG weight rounds + (min(M, 8 NT) + 1) activation rows
     XchgArgs xa;      // world > 0: fp32 partials go to the tensor-parallel exchange
     int act;          // 1: SwiGLU over interleaved gate/up rows (y has N / 2 columns)
+    int pdl_early;    // pipe kernel: signal dependents at the start instead of the end
 };
 
 // SwiGLU epilogue.  The matrix holds gate and up rows interleaved in blocks of 8
@@ -326,6 +329,15 @@ struct PipeStage {
     static int bytes(int m) { return RG * kWBytes + (m + 1) * kXStride; }
 };
 
+// Programmatic dependent launch (no-ops when the launch did not ask for it):
+// griddepcontrol.wait blocks until the previous kernel in the stream has
+// completed and its writes are visible; launch_dependents lets the next
+// kernel's CTAs be scheduled once every CTA of this grid has signalled it.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // RG row groups per CTA (consumer warp w: row group w / 8, tile 8r + w % 8);
 // every consumer of a round reads the same activation slice, so activation
 // traffic per weight falls by RG.  Requires K % 64 == 0 (the generic kernel
@@ -362,21 +374,20 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
     fence_proxy_async_smem();
     __syncthreads();
 
+    if (a.pdl_early) pdl_trigger();
     if (warp == kConsumers) {
         // ---------------- producer warp ----------------
-        int st = 0, ph = 0;
-        for (int r = 0; r < rounds; ++r, st = (st + 1 == D ? 0 : st + 1), ph ^= (st == 0)) {
-            if (r >= D && !bounded_wait(smem_u32(&empty[st]), uint32_t(ph ^ 1))) {
-                if (lane == 0) atomicExch(&g_device_status, kDeviceTimeout);
-                break;
-            }
+        // The weight bytes of the first D rounds are requested before
+        // griddepcontrol.wait (weights never depend on the previous kernel), their
+        // activation slices after it.
+        int ngroups = 0;
+#pragma unroll
+        for (int rg = 0; rg < RG; ++rg) ngroups += (blockIdx.x * RG + rg) < a.groups ? 1 : 0;
+        auto weights = [&](int r, int st) {
             const int ntile = min(S::kRound, a.kt - r * S::kRound);
             const uint32_t xbytes = uint32_t(ntile * kKTile * 2);
             uint8_t* dst = smem + st * SB;
             const uint32_t bar = smem_u32(&full[st]);
-            int ngroups = 0;
-#pragma unroll
-            for (int rg = 0; rg < RG; ++rg) ngroups += (blockIdx.x * RG + rg) < a.groups ? 1 : 0;
             if (lane == 0) {
                 mbar_expect_tx(bar, uint32_t(ngroups * ntile * S::kTileBytes) + xbytes * uint32_t(mrows));
 #pragma unroll
@@ -388,11 +399,31 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
                                  uint32_t(ntile * S::kTileBytes), bar);
                 }
             }
-            __syncwarp();
+        };
+        auto acts = [&](int r, int st) {
+            const int ntile = min(S::kRound, a.kt - r * S::kRound);
             if (lane < mrows)
-                bulk_g2s(smem_u32(dst + RG * S::kWBytes + lane * S::kXStride),
-                         a.x + size_t(lane) * a.K + size_t(r) * S::kRound * kKTile, xbytes, bar);
+                bulk_g2s(smem_u32(smem + st * SB + RG * S::kWBytes + lane * S::kXStride),
+                         a.x + size_t(lane) * a.K + size_t(r) * S::kRound * kKTile,
+                         uint32_t(ntile * kKTile * 2), smem_u32(&full[st]));
+        };
+        const int pre = rounds < D ? rounds : D;
+        for (int r = 0; r < pre; ++r) weights(r, r);
+        pdl_wait();
+        __syncwarp();
+        for (int r = 0; r < pre; ++r) acts(r, r);
+        for (int r = pre; r < rounds; ++r) {
+            const int st = r % D;
+            const uint32_t ph = uint32_t(r / D) & 1u;
+            if (!bounded_wait(smem_u32(&empty[st]), ph ^ 1u)) {
+                if (lane == 0) atomicExch(&g_device_status, kDeviceTimeout);
+                break;
+            }
+            weights(r, st);
+            __syncwarp();
+            acts(r, st);
         }
+        if (!a.pdl_early) pdl_trigger();
     } else {
         // ---------------- consumer warps ----------------
         const int rgl = warp / kWarps;   // local row group
@@ -403,8 +434,22 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
         const int c = lane & 3;
         const int row_lo = g * kRowGroup + r0;
         const uint32_t magic = a.magic;  // opaque: kept in a register, never re-materialised
+        // b = 8..12 (fullPrecision): paired f32x2 decode with the row scale itself
+        constexpr bool kPaired = !HW && B >= 8 && B <= 12;
+        constexpr int kPB = kPaired ? B : 8;
+        PairConsts<kPB> pk;
+        uint64_t s2[2] = {0, 0};
+        if constexpr (kPaired) {
+            pk.init(magic);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int row = row_lo + 8 * h;
+                const float sv = (grp_ok && row < a.N) ? a.scales[row] : 0.0f;
+                s2[h] = pack2f(sv, sv);
+            }
+        }
         float sc[2][kMaxSlots];
-        if constexpr (B != kFp16Bits && !HW) {
+        if constexpr (B != kFp16Bits && !HW && !kPaired) {
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const int row = row_lo + 8 * h;
@@ -475,46 +520,63 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
                 if (lane == 0) mbar_arrive(smem_u32(&empty[st]));
             }
             if (!have) continue;
+            if constexpr (kPaired) {
+                // k-steps 0 and 2, then 1 and 3, share their decode pairs
 #pragma unroll
-            for (int s = 0; s < 4; ++s) {
-                uint32_t af[4];
-                if constexpr (B == kFp16Bits) {
+                for (int sp = 0; sp < 2; ++sp) {
+                    uint32_t af_lo[4], af_hi[4];
+                    if (sp == 0)
+                        dequant_steps<kPB, 0>(reinterpret_cast<const uint32_t(&)[kPB]>(w), pk, s2, af_lo, af_hi);
+                    else
+                        dequant_steps<kPB, 1>(reinterpret_cast<const uint32_t(&)[kPB]>(w), pk, s2, af_lo, af_hi);
 #pragma unroll
-                    for (int rr = 0; rr < 4; ++rr) af[rr] = w[4 * s + rr];
-                } else {
-                    // pair p = 4s + rr holds codes 2p, 2p+1; rr odd -> row r0+8
-#define EBX_PAIR(RR)                                                                               \
-    do {                                                                                           \
-        constexpr int J = 2 * (4 * S_ + RR);                                                       \
-        float lo, hi;                                                                              \
-        if constexpr (HW) {                                                                        \
-            lo = decode_code_int<B, J>(w, magic);                                                  \
-            hi = decode_code_int<B, J + 1>(w, magic);                                              \
-        } else {                                                                                   \
-            lo = decode_code<B, J, DIRECT>(w, sc[RR & 1], magic);                                  \
-            hi = decode_code<B, J + 1, DIRECT>(w, sc[RR & 1], magic);                              \
-        }                                                                                          \
-        af[RR] = pack_half2(lo, hi);                                                               \
-    } while (0)
-                    switch (s) {
-#define EBX_STEP(SS)                    \
-    case SS: {                          \
-        constexpr int S_ = SS;          \
-        EBX_PAIR(0);                    \
-        EBX_PAIR(1);                    \
-        EBX_PAIR(2);                    \
-        EBX_PAIR(3);                    \
-        break;                          \
-    }
-                        EBX_STEP(0) EBX_STEP(1) EBX_STEP(2) EBX_STEP(3)
-#undef EBX_STEP
-#undef EBX_PAIR
+                    for (int nb = 0; nb < NT; ++nb) {
+                        mma_16816(acc[nb], af_lo, xb[nb][sp * 2], xb[nb][sp * 2 + 1]);
+                        mma_16816(acc[nb], af_hi, xb[nb][4 + sp * 2], xb[nb][4 + sp * 2 + 1]);
                     }
                 }
+            } else {
 #pragma unroll
-                for (int nb = 0; nb < NT; ++nb)
-                    mma_16816(acc[nb], af, xb[nb][(s >> 1) * 4 + (s & 1) * 2],
-                              xb[nb][(s >> 1) * 4 + (s & 1) * 2 + 1]);
+                for (int s = 0; s < 4; ++s) {
+                    uint32_t af[4];
+                    if constexpr (B == kFp16Bits) {
+#pragma unroll
+                        for (int rr = 0; rr < 4; ++rr) af[rr] = w[4 * s + rr];
+                    } else {
+                        // pair p = 4s + rr holds codes 2p, 2p+1; rr odd -> row r0+8
+#define EBX_PAIR(RR)                                                                               \
+        do {                                                                                           \
+            constexpr int J = 2 * (4 * S_ + RR);                                                       \
+            float lo, hi;                                                                              \
+            if constexpr (HW) {                                                                        \
+                lo = decode_code_int<B, J>(w, magic);                                                  \
+                hi = decode_code_int<B, J + 1>(w, magic);                                              \
+            } else {                                                                                   \
+                lo = decode_code<B, J, DIRECT>(w, sc[RR & 1], magic);                                  \
+                hi = decode_code<B, J + 1, DIRECT>(w, sc[RR & 1], magic);                              \
+            }                                                                                          \
+            af[RR] = pack_half2(lo, hi);                                                               \
+        } while (0)
+                        switch (s) {
+#define EBX_STEP(SS)                    \
+        case SS: {                          \
+            constexpr int S_ = SS;          \
+            EBX_PAIR(0);                    \
+            EBX_PAIR(1);                    \
+            EBX_PAIR(2);                    \
+            EBX_PAIR(3);                    \
+            break;                          \
+        }
+                            EBX_STEP(0) EBX_STEP(1) EBX_STEP(2) EBX_STEP(3)
+#undef EBX_STEP
+#undef EBX_PAIR
+                        }
+                    }
+#pragma unroll
+                    for (int nb = 0; nb < NT; ++nb)
+                        mma_16816(acc[nb], af, xb[nb][(s >> 1) * 4 + (s & 1) * 2],
+                                  xb[nb][(s >> 1) * 4 + (s & 1) * 2 + 1]);
+                }
             }
           }
         }
@@ -523,7 +585,9 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
 #pragma unroll
             for (int i = 0; i < 4; ++i)
                 red[(((rgl * kWarps + wt) * NT + nb) * 32 + lane) * 4 + i] = acc[nb][i];
+        if (!a.pdl_early) pdl_trigger();
     }
+    pdl_wait();  // outputs may alias the previous kernel's buffers
     __syncthreads();
     for (int idx = threadIdx.x; idx < RG * NT * 128; idx += blockDim.x) {
         const int rgl = idx / (NT * 128);
@@ -574,16 +638,46 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
 
 constexpr int kStages = 4;
 
+// Runtime knobs of the decode launcher, read once per process:
+//   EBX_PDL=0             launch without programmatic dependent launch
+//   EBX_PDL_TRIGGER=early signal dependents at the start of each CTA (default:
+//                         once its main loop is done)
+struct DecodeKnobs {
+    bool pdl = true;
+    bool early = false;
+};
+const DecodeKnobs& decode_knobs() {
+    static const DecodeKnobs k = [] {
+        DecodeKnobs v;
+        if (const char* e = std::getenv("EBX_PDL")) v.pdl = std::atoi(e) != 0;
+        if (const char* e = std::getenv("EBX_PDL_TRIGGER")) v.early = std::strcmp(e, "early") == 0;
+        return v;
+    }();
+    return k;
+}
+
 // Exchange launches: fused (reduce inside the decode kernel) only when the whole
 // grid fits on the GPU at once; the launch is then cooperative, which makes the
 // runtime guarantee that co-residency, so CTAs that wait for peers' partials can
 // never hold back CTAs of their own grid that those peers wait for in turn.
 template <typename Kern>
 cudaError_t launch_maybe_xchg(Kern kern, DecodeArgs& a, unsigned grid, unsigned threads, int smem,
-                              cudaStream_t s) {
+                              cudaStream_t s, bool pdl = false) {
     if (!a.xa.world) {
-        kern<<<grid, threads, smem, s>>>(a);
-        return cudaGetLastError();
+        // pdl: the kernel waits (griddepcontrol.wait) before it reads anything the
+        // previous kernel may write, so it may be launched before that one completes
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(grid);
+        cfg.blockDim = dim3(threads);
+        cfg.dynamicSmemBytes = size_t(smem);
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = pdl && decode_knobs().pdl ? 1 : 0;
+        a.pdl_early = decode_knobs().early ? 1 : 0;
+        return cudaLaunchKernelEx(&cfg, kern, a);
     }
     int dev = 0, sms = 0, per_sm = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -652,7 +746,8 @@ cudaError_t launch_pipe(DecodeArgs& a, int groups, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         configured.fetch_or(bit);
     }
-    return launch_maybe_xchg(kern, a, unsigned((groups + RG - 1) / RG), kThreads * RG + 32, smem, s);
+    return launch_maybe_xchg(kern, a, unsigned((groups + RG - 1) / RG), kThreads * RG + 32, smem, s,
+                             true);
 }
 
 template <int B, bool HW>
@@ -724,6 +819,7 @@ cudaError_t launch_decode(const Matrix& m, const uint16_t* x, int64_t M, const u
         const int groups = int(m.groups);
         cudaError_t e = cudaErrorInvalidValue;
         const bool v = vecx && ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0);
+        a.pdl_early = 0;
         switch (m.bits) {
 #define EBX_DEC_CASE(BB)                                                                \
     case BB:                                                                            \
