@@ -250,6 +250,27 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4],
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// Shared-memory loads at 32-bit shared addresses.  volatile: they must stay
+// after the mbarrier wait that makes the data valid (and before the arrive
+// that releases the slot), which are volatile asm statements too.
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -482,20 +503,25 @@ template <int B, int S>
 __device__ __forceinline__ void dequant_steps(const uint32_t (&w)[B], const PairConsts<B>& k,
                                               const uint64_t (&s2)[2], uint32_t (&af_lo)[4],
                                               uint32_t (&af_hi)[4]) {
-    float fl[8], fh[8];
-    dequant_pair<B, 8 * S + 0>(w, k, s2[0], fl[0], fh[0]);
-    dequant_pair<B, 8 * S + 1>(w, k, s2[0], fl[1], fh[1]);
-    dequant_pair<B, 8 * S + 2>(w, k, s2[1], fl[2], fh[2]);
-    dequant_pair<B, 8 * S + 3>(w, k, s2[1], fl[3], fh[3]);
-    dequant_pair<B, 8 * S + 4>(w, k, s2[0], fl[4], fh[4]);
-    dequant_pair<B, 8 * S + 5>(w, k, s2[0], fl[5], fh[5]);
-    dequant_pair<B, 8 * S + 6>(w, k, s2[1], fl[6], fh[6]);
-    dequant_pair<B, 8 * S + 7>(w, k, s2[1], fl[7], fh[7]);
-#pragma unroll
-    for (int rr = 0; rr < 4; ++rr) {
-        af_lo[rr] = pack_half2(fl[2 * rr], fl[2 * rr + 1]);
-        af_hi[rr] = pack_half2(fh[2 * rr], fh[2 * rr + 1]);
-    }
+    // register rr = codes 2rr, 2rr + 1: packed as soon as its two pairs are done
+    // (keeps at most four unpacked floats live)
+    float l0, l1, h0, h1;
+    dequant_pair<B, 8 * S + 0>(w, k, s2[0], l0, h0);
+    dequant_pair<B, 8 * S + 1>(w, k, s2[0], l1, h1);
+    af_lo[0] = pack_half2(l0, l1);
+    af_hi[0] = pack_half2(h0, h1);
+    dequant_pair<B, 8 * S + 2>(w, k, s2[1], l0, h0);
+    dequant_pair<B, 8 * S + 3>(w, k, s2[1], l1, h1);
+    af_lo[1] = pack_half2(l0, l1);
+    af_hi[1] = pack_half2(h0, h1);
+    dequant_pair<B, 8 * S + 4>(w, k, s2[0], l0, h0);
+    dequant_pair<B, 8 * S + 5>(w, k, s2[0], l1, h1);
+    af_lo[2] = pack_half2(l0, l1);
+    af_hi[2] = pack_half2(h0, h1);
+    dequant_pair<B, 8 * S + 6>(w, k, s2[1], l0, h0);
+    dequant_pair<B, 8 * S + 7>(w, k, s2[1], l1, h1);
+    af_lo[3] = pack_half2(l0, l1);
+    af_hi[3] = pack_half2(h0, h1);
 }
 
 }  // namespace ebx

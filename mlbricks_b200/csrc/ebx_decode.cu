@@ -470,54 +470,62 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
         for (int nb = 0; nb < NT; ++nb)
 #pragma unroll
             for (int i = 0; i < 4; ++i) acc[nb][i] = 0.0f;
+        // Shared-memory addresses (32-bit) of this lane's operands in stage 0; a
+        // round adds the stage offset `so`.  Weight words sit at q*512 + lane*16
+        // (16-byte segments), then lane*8 and lane*4 (see ebx_common.cuh).
+        const uint32_t wb = smem_u32(smem) + uint32_t(rgl * S::kWBytes + wt * TPW * S::kTileBytes);
+        const uint32_t w16 = wb + uint32_t(lane * 16), w8 = wb + uint32_t(lane * 8),
+                       w4 = wb + uint32_t(lane * 4);
         // activation row of token r0 + 8 nb, or the zero row when that token >= M
-        const uint8_t* xrow[NT];
+        uint32_t xa[NT];
 #pragma unroll
         for (int nb = 0; nb < NT; ++nb) {
             const int tok = r0 + 8 * nb;
-            xrow[nb] = smem + RG * S::kWBytes + (tok < mrows ? tok : mrows) * S::kXStride +
-                       wt * TPW * kKTile * 2 + 32 * c;
+            xa[nb] = smem_u32(smem) + uint32_t(RG * S::kWBytes + (tok < mrows ? tok : mrows) * S::kXStride +
+                                               wt * TPW * kKTile * 2 + 32 * c);
         }
-
-        int st = 0, ph = 0;
-        for (int r = 0; r < rounds; ++r, st = (st + 1 == D ? 0 : st + 1), ph ^= (st == 0)) {
-            if (!bounded_wait(smem_u32(&full[st]), uint32_t(ph))) {
+        const uint32_t full0 = smem_u32(&full[0]), empty0 = smem_u32(&empty[0]);
+        // tiles of this warp's slot still ahead of the current round
+        int rem = grp_ok ? a.kt - wt * TPW : 0;
+        uint32_t so = 0;
+        int st = 0;
+        uint32_t ph = 0;
+        for (int r = 0; r < rounds; ++r) {
+            if (!bounded_wait(full0 + 8u * uint32_t(st), ph)) {
                 if (lane == 0) atomicExch(&g_device_status, kDeviceTimeout);
                 break;
             }
 #pragma unroll
           for (int j = 0; j < TPW; ++j) {
-            const bool have = grp_ok && (r * S::kRound + wt * TPW + j < a.kt);
-            const uint8_t* sw = smem + st * SB + rgl * S::kWBytes + (wt * TPW + j) * S::kTileBytes;
+            const bool have = rem > j;
             uint32_t w[B];
             uint32_t xb[NT][8];
             if (have) {
+                const int T0 = j * S::kTileBytes;
 #pragma unroll
                 for (int q = 0; q < B / 4; ++q) {
-                    const uint4 v = *reinterpret_cast<const uint4*>(sw + q * 512 + lane * 16);
+                    const uint4 v = lds128(w16 + so + uint32_t(T0 + q * 512));
                     w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
                 }
                 if constexpr ((B & 2) != 0) {
-                    const uint2 v = *reinterpret_cast<const uint2*>(sw + (B / 4) * 512 + lane * 8);
+                    const uint2 v = lds64(w8 + so + uint32_t(T0 + (B / 4) * 512));
                     w[4 * (B / 4)] = v.x;
                     w[4 * (B / 4) + 1] = v.y;
                 }
                 if constexpr ((B & 1) != 0)
-                    w[B - 1] = *reinterpret_cast<const uint32_t*>(sw + (B / 4) * 512 +
-                                                                  ((B & 2) ? 256 : 0) + lane * 4);
+                    w[B - 1] = lds32(w4 + so + uint32_t(T0 + (B / 4) * 512 + ((B & 2) ? 256 : 0)));
 #pragma unroll
                 for (int nb = 0; nb < NT; ++nb)
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
-                        const uint4 v = *reinterpret_cast<const uint4*>(xrow[nb] + st * SB +
-                                                                        j * kKTile * 2 + 16 * h);
+                        const uint4 v = lds128(xa[nb] + so + uint32_t(j * kKTile * 2 + 16 * h));
                         xb[nb][4 * h] = v.x; xb[nb][4 * h + 1] = v.y;
                         xb[nb][4 * h + 2] = v.z; xb[nb][4 * h + 3] = v.w;
                     }
             }
             if (j == TPW - 1) {  // every load of this stage has been issued
                 __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(&empty[st]));
+                if (lane == 0) mbar_arrive(empty0 + 8u * uint32_t(st));
             }
             if (!have) continue;
             if constexpr (kPaired) {
@@ -579,6 +587,13 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
                 }
             }
           }
+            rem -= S::kRound;
+            so += uint32_t(SB);
+            if (++st == D) {
+                st = 0;
+                so = 0;
+                ph ^= 1u;
+            }
         }
 #pragma unroll
         for (int nb = 0; nb < NT; ++nb)
@@ -642,18 +657,42 @@ constexpr int kStages = 4;
 //   EBX_PDL=0             launch without programmatic dependent launch
 //   EBX_PDL_TRIGGER=early signal dependents at the start of each CTA (default:
 //                         once its main loop is done)
+//   EBX_M4_MINB=2|3       M <= 4: CTAs per SM (default: 2 when the grid is then one
+//                         wave and K <= 8192, else 3)
+//   EBX_M8_MINB=2|3       4 < M <= 8: CTAs per SM (default 2: two supertiles per
+//                         warp and round; 3: one)
+//   EBX_M16_MINB=2|3      8 < M <= 16: CTAs per SM (default: as for M <= 4)
 struct DecodeKnobs {
     bool pdl = true;
     bool early = false;
+    int m4_minb = 0;
+    int m8_minb = 2;
+    int m16_minb = 0;
 };
 const DecodeKnobs& decode_knobs() {
     static const DecodeKnobs k = [] {
         DecodeKnobs v;
         if (const char* e = std::getenv("EBX_PDL")) v.pdl = std::atoi(e) != 0;
         if (const char* e = std::getenv("EBX_PDL_TRIGGER")) v.early = std::strcmp(e, "early") == 0;
+        if (const char* e = std::getenv("EBX_M4_MINB")) v.m4_minb = std::atoi(e) == 2 ? 2 : 3;
+        if (const char* e = std::getenv("EBX_M8_MINB")) v.m8_minb = std::atoi(e) == 3 ? 3 : 2;
+        if (const char* e = std::getenv("EBX_M16_MINB")) v.m16_minb = std::atoi(e) == 2 ? 2 : 3;
         return v;
     }();
     return k;
+}
+
+// Multiprocessors of the current device (cached per device).
+int sm_count() {
+    static std::atomic<int> cache[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    int n = cache[dev & 63].load(std::memory_order_relaxed);
+    if (n == 0) {
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+        cache[dev & 63].store(n, std::memory_order_relaxed);
+    }
+    return n;
 }
 
 // Exchange launches: fused (reduce inside the decode kernel) only when the whole
@@ -675,7 +714,9 @@ cudaError_t launch_maybe_xchg(Kern kern, DecodeArgs& a, unsigned grid, unsigned 
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
-        cfg.numAttrs = pdl && decode_knobs().pdl ? 1 : 0;
+        // measured: overlapping helps when a CTA's run is short (K <= 8192) and costs
+        // 5-8 % when it is long (K = 14336: next grid's CTAs land unevenly)
+        cfg.numAttrs = pdl && decode_knobs().pdl && a.kt <= 128 ? 1 : 0;
         a.pdl_early = decode_knobs().early ? 1 : 0;
         return cudaLaunchKernelEx(&cfg, kern, a);
     }
@@ -720,13 +761,13 @@ cudaError_t launch_one(DecodeArgs& a, int groups, cudaStream_t s) {
     return launch_maybe_xchg(kern, a, unsigned(groups), kThreads, smem, s);
 }
 
-template <int B, bool HW, int NT, bool DIRECT, int RG, int TPW>
+template <int B, bool HW, int NT, bool DIRECT, int RG, int TPW, int MINB = (RG == 1 ? 3 : 1)>
 cudaError_t launch_pipe(DecodeArgs& a, int groups, cudaStream_t s) {
     using S = PipeStage<B, NT, RG, TPW>;
-    // RG == 1: three CTAs per SM (27 warps); RG == 2: one CTA per SM.  The ring
-    // is as deep as that budget allows for this M (2..kMaxStages stages).
-    constexpr int MINB = RG == 1 ? 3 : 1;
-    constexpr int kBudget = RG == 1 ? 74 * 1024 : 215 * 1024;
+    // MINB CTAs per SM share its shared memory (three: 27 warps; two: 18; RG == 2:
+    // one CTA of 17 warps).  The ring is as deep as that budget allows for this M
+    // (2..kMaxStages stages).
+    constexpr int kBudget = MINB == 3 ? 74 * 1024 : (MINB == 2 ? 110 * 1024 : 215 * 1024);
     constexpr int kFixed = 2 * kMaxStages * 8 + S::kRedBytes + 16;
     const int mrows = a.M < NT * 8 ? a.M : NT * 8;
     a.stage_bytes = S::bytes(mrows);
@@ -758,19 +799,36 @@ cudaError_t dispatch_nt(DecodeArgs& a, int groups, bool pipe, bool direct, cudaS
         // M <= 8: one per warp; M <= 16: one row group per CTA with 16 activation rows
         // (two stages; measured faster than two row groups per CTA at one CTA per SM,
         // whose 448-CTA grid for N = 14336 runs in 3.03 waves).
-        constexpr bool kCanDirect = !HW && B != kFp16Bits;
+        // (8..12-bit full semantics decode in pairs and ignore `direct`)
+        constexpr bool kCanDirect = !HW && B != kFp16Bits && !(B >= 8 && B <= 12);
+        const DecodeKnobs& kn = decode_knobs();
+        // Two CTAs per SM (a deeper ring, up to 113 registers) pay off when the grid
+        // is then still one wave and each CTA's run is short (measured on the
+        // BASELINE shapes: 4096x4096 12 % faster; 14336-row and 14336-column
+        // matrices slower), else three CTAs per SM.
+        const bool two_per_sm = groups <= 2 * sm_count() && a.kt <= 128;
         if (B <= 12 && a.M <= 4) {
+            if (kn.m4_minb == 2 || (kn.m4_minb == 0 && two_per_sm))
+                return launch_pipe<B, HW, 1, false, 1, 2, 2>(a, groups, s);
             if constexpr (kCanDirect)
                 if (direct) return launch_pipe<B, HW, 1, true, 1, 2>(a, groups, s);
             return launch_pipe<B, HW, 1, false, 1, 2>(a, groups, s);
         }
         if (a.M <= 8) {
+            // two CTAs per SM with two supertiles per warp and round (measured 13-22 %
+            // faster than three CTAs with one supertile on the BASELINE decode shapes)
+            if constexpr (B <= 12)
+                if (kn.m8_minb == 2) return launch_pipe<B, HW, 1, false, 1, 2, 2>(a, groups, s);
             if constexpr (kCanDirect)
                 if (direct) return launch_pipe<B, HW, 1, true, 1, 1>(a, groups, s);
             return launch_pipe<B, HW, 1, false, 1, 1>(a, groups, s);
         }
         if constexpr (B == kFp16Bits)  // 16-bit weights: two stages need the larger budget
             return launch_pipe<B, HW, 2, false, 2, 1>(a, groups, s);
+        // 16 activation rows: two CTAs per SM (a three-stage ring) under the same
+        // rule, else three CTAs per SM (two stages)
+        if (kn.m16_minb == 2 || (kn.m16_minb == 0 && two_per_sm))
+            return launch_pipe<B, HW, 2, false, 1, 1, 2>(a, groups, s);
         if constexpr (kCanDirect)
             if (direct) return launch_pipe<B, HW, 2, true, 1, 1>(a, groups, s);
         return launch_pipe<B, HW, 2, false, 1, 1>(a, groups, s);
