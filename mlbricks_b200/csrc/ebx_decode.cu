@@ -470,24 +470,24 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
         for (int nb = 0; nb < NT; ++nb)
 #pragma unroll
             for (int i = 0; i < 4; ++i) acc[nb][i] = 0.0f;
-        // Shared-memory addresses (32-bit) of this lane's operands in stage 0; a
-        // round adds the stage offset `so`.  Weight words sit at q*512 + lane*16
-        // (16-byte segments), then lane*8 and lane*4 (see ebx_common.cuh).
-        const uint32_t wb = smem_u32(smem) + uint32_t(rgl * S::kWBytes + wt * TPW * S::kTileBytes);
-        const uint32_t w16 = wb + uint32_t(lane * 16), w8 = wb + uint32_t(lane * 8),
-                       w4 = wb + uint32_t(lane * 4);
+        // Byte offsets (in the dynamic shared array) of this lane's operands in
+        // stage 0; a round adds the stage offset `so`.  Weight words sit at
+        // q*512 + lane*16 (16-byte segments), then lane*8 and lane*4 (see
+        // ebx_common.cuh).
+        const int wb = rgl * S::kWBytes + wt * TPW * S::kTileBytes;
+        const int w16 = wb + lane * 16, w8 = wb + lane * 8, w4 = wb + lane * 4;
         // activation row of token r0 + 8 nb, or the zero row when that token >= M
-        uint32_t xa[NT];
+        int xa[NT];
 #pragma unroll
         for (int nb = 0; nb < NT; ++nb) {
             const int tok = r0 + 8 * nb;
-            xa[nb] = smem_u32(smem) + uint32_t(RG * S::kWBytes + (tok < mrows ? tok : mrows) * S::kXStride +
-                                               wt * TPW * kKTile * 2 + 32 * c);
+            xa[nb] = RG * S::kWBytes + (tok < mrows ? tok : mrows) * S::kXStride + wt * TPW * kKTile * 2 +
+                     32 * c;
         }
         const uint32_t full0 = smem_u32(&full[0]), empty0 = smem_u32(&empty[0]);
         // tiles of this warp's slot still ahead of the current round
         int rem = grp_ok ? a.kt - wt * TPW : 0;
-        uint32_t so = 0;
+        int so = 0;
         int st = 0;
         uint32_t ph = 0;
         for (int r = 0; r < rounds; ++r) {
@@ -504,21 +504,23 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
                 const int T0 = j * S::kTileBytes;
 #pragma unroll
                 for (int q = 0; q < B / 4; ++q) {
-                    const uint4 v = lds128(w16 + so + uint32_t(T0 + q * 512));
+                    const uint4 v = *reinterpret_cast<const uint4*>(smem + w16 + so + T0 + q * 512);
                     w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
                 }
                 if constexpr ((B & 2) != 0) {
-                    const uint2 v = lds64(w8 + so + uint32_t(T0 + (B / 4) * 512));
+                    const uint2 v = *reinterpret_cast<const uint2*>(smem + w8 + so + T0 + (B / 4) * 512);
                     w[4 * (B / 4)] = v.x;
                     w[4 * (B / 4) + 1] = v.y;
                 }
                 if constexpr ((B & 1) != 0)
-                    w[B - 1] = lds32(w4 + so + uint32_t(T0 + (B / 4) * 512 + ((B & 2) ? 256 : 0)));
+                    w[B - 1] = *reinterpret_cast<const uint32_t*>(smem + w4 + so + T0 + (B / 4) * 512 +
+                                                                  ((B & 2) ? 256 : 0));
 #pragma unroll
                 for (int nb = 0; nb < NT; ++nb)
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
-                        const uint4 v = lds128(xa[nb] + so + uint32_t(j * kKTile * 2 + 16 * h));
+                        const uint4 v = *reinterpret_cast<const uint4*>(smem + xa[nb] + so + j * kKTile * 2 +
+                                                                        16 * h);
                         xb[nb][4 * h] = v.x; xb[nb][4 * h + 1] = v.y;
                         xb[nb][4 * h + 2] = v.z; xb[nb][4 * h + 3] = v.w;
                     }
@@ -588,7 +590,7 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
             }
           }
             rem -= S::kRound;
-            so += uint32_t(SB);
+            so += SB;
             if (++st == D) {
                 st = 0;
                 so = 0;
