@@ -283,6 +283,8 @@ def run_gpu(args) -> None:
     del mats, handles, launches
     torch.cuda.empty_cache()
     tp_stack = None if args.no_tp_stack else run_tp_stack(args, world, rank, device)
+    # config 4: the compressed BoltModel-shaped decoder (rank 0's GPU of the replicas)
+    bolt = run_bolt_decoder(device) if not args.no_bolt and rank == 0 else None
 
     result = {
         "metric": METRIC,
@@ -319,6 +321,7 @@ def run_gpu(args) -> None:
         "e2e": e2e,
         "prefill": prefill,
         "tp_stack": tp_stack,
+        "bolt_decoder": bolt,
         "gpu_launches": nL * args.steps,
         "clocks": clocks,
     }
@@ -596,6 +599,189 @@ def run_e2e(mats, device, args) -> dict:
 
 
 # ---------------------------------------------------------------------------
+# compressed small BoltModel-shaped decoder
+# ---------------------------------------------------------------------------
+BOLT = dict(vocab=32000, dim=384, heads=12, kv_heads=1, layers=6, ffn_mult=4, batch=8,
+            prefill=512, steps=128)
+
+
+def _bolt_model(device):
+    """BoltModel-shaped decoder (vocab 32000, dim 384, 12 query heads over one shared
+    key/value head, 6 pre-norm layers, FFN 4x with GELU, RMSNorm, tied FP16 output
+    head), N(0, 0.02) init, FP16.  Attention is plain multi-query scaled-dot-product
+    attention over a key/value cache; BOLT's own attention variants are not on the
+    compressed-linear path, every projection and FFN matrix is."""
+    import torch
+    import torch.nn as nn
+    import torch.nn.functional as F
+
+    c = BOLT
+    hd = c["dim"] // c["heads"]
+
+    class Block(nn.Module):
+        def __init__(self):
+            super().__init__()
+            d = c["dim"]
+            self.n1 = nn.RMSNorm(d, eps=1e-6)
+            self.q = nn.Linear(d, d, bias=False)
+            self.k = nn.Linear(d, hd * c["kv_heads"], bias=False)
+            self.v = nn.Linear(d, hd * c["kv_heads"], bias=False)
+            self.o = nn.Linear(d, d, bias=False)
+            self.n2 = nn.RMSNorm(d, eps=1e-6)
+            self.up = nn.Linear(d, c["ffn_mult"] * d, bias=False)
+            self.down = nn.Linear(c["ffn_mult"] * d, d, bias=False)
+
+        def forward(self, h, kc, vc, pos):
+            # h [B, T, d]; kc / vc [B, 1, L, hd] caches; pos: positions of these T tokens
+            B, T, _ = h.shape
+            a = self.n1(h)
+            q = self.q(a).view(B, T, c["heads"], hd).transpose(1, 2)
+            k = self.k(a).view(B, T, 1, hd).transpose(1, 2)
+            v = self.v(a).view(B, T, 1, hd).transpose(1, 2)
+            kc.index_copy_(2, pos, k)
+            vc.index_copy_(2, pos, v)
+            if T > 1:  # prefill from position 0: causal attention over these tokens
+                att = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+            else:      # one new token: attend to cache positions <= pos
+                L = kc.shape[2]
+                s = (q @ kc.transpose(-1, -2)) * (hd ** -0.5)
+                mask = torch.arange(L, device=h.device) > pos
+                att = torch.softmax(s.float().masked_fill(mask, float("-inf")), -1).to(vc.dtype) @ vc
+            h = h + self.o(att.transpose(1, 2).reshape(B, T, -1))
+            return h + self.down(F.gelu(self.up(self.n2(h))))
+
+    class Decoder(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.embed = nn.Embedding(c["vocab"], c["dim"])
+            self.blocks = nn.ModuleList([Block() for _ in range(c["layers"])])
+            self.norm = nn.RMSNorm(c["dim"], eps=1e-6)
+            self.lm_head = nn.Linear(c["dim"], c["vocab"], bias=False)
+            self.lm_head.weight = self.embed.weight  # tied: stays FP16 under ElasticBit
+
+        def get_output_embeddings(self):
+            return self.lm_head
+
+        def step(self, ids, caches, pos):
+            h = self.embed(ids)
+            for blk, (kc, vc) in zip(self.blocks, caches):
+                h = blk(h, kc, vc, pos)
+            return self.lm_head(self.norm(h[:, -1]))
+
+        def forward(self, ids):  # calibration / plain use: a fresh cache
+            caches = self.new_caches(ids.shape[0], ids.device)
+            return self.step(ids, caches, torch.arange(ids.shape[1], device=ids.device))
+
+        def new_caches(self, B, dev):
+            L = c["prefill"] + c["steps"]
+            return [(torch.zeros(B, 1, L, hd, dtype=torch.float16, device=dev),
+                     torch.zeros(B, 1, L, hd, dtype=torch.float16, device=dev))
+                    for _ in range(c["layers"])]
+
+    g = torch.Generator().manual_seed(4)
+    m = Decoder()
+    with torch.no_grad():
+        for p in m.parameters():
+            if p.dim() >= 2:
+                p.copy_(torch.randn(p.shape, generator=g) * 0.02)
+    return m.to(device).half().eval()
+
+
+def _bolt_generate(model, ids, device):
+    """512-token prefill, then BOLT['steps'] greedy steps replayed from one CUDA graph.
+    Returns (prefill ms, decode ms, generated ids)."""
+    import torch
+
+    c = BOLT
+    B = ids.shape[0]
+    caches = model.new_caches(B, device)
+    with torch.inference_mode():
+        for _ in range(2):  # warm-up (kernels configured, allocator pools sized)
+            model.step(ids, caches, torch.arange(c["prefill"], device=device))
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        logits = model.step(ids, caches, torch.arange(c["prefill"], device=device))
+        b.record()
+        b.synchronize()
+        prefill_ms = a.elapsed_time(b)
+        tok = logits.argmax(-1, keepdim=True)
+        pos = torch.full((1,), c["prefill"], dtype=torch.int64, device=device)
+        out = torch.empty((B, c["steps"]), dtype=torch.int64, device=device)
+        col = torch.zeros((1,), dtype=torch.int64, device=device)
+        s = torch.cuda.Stream(device)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):  # warm-up outside the graph (state restored below)
+                model.step(tok, caches, pos)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            nxt = model.step(tok, caches, pos).argmax(-1, keepdim=True)
+            out.index_copy_(1, col, nxt)
+            tok.copy_(nxt)
+            pos.add_(1)
+            col.add_(1)
+        # restart the generation from the prefill state
+        model.step(ids, caches, torch.arange(c["prefill"], device=device))
+        tok.copy_(logits.argmax(-1, keepdim=True))
+        pos.fill_(c["prefill"])
+        col.zero_()
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(c["steps"]):
+            graph.replay()
+        b.record()
+        b.synchronize()
+        decode_ms = a.elapsed_time(b)
+        del graph
+    return prefill_ms, decode_ms, out
+
+
+def run_bolt_decoder(device) -> dict:
+    """the BoltModel-shaped decoder, dense FP16 and ElasticBit-
+    compressed (every projection/FFN Linear at threshold 0.01, native route, tied head
+    kept FP16 as the reference does), batch 8, 512-token prefill of uniform random
+    ids, 128 greedy steps; tok/s of prefill and decode."""
+    import copy
+
+    import torch
+
+    from mlbricks_b200 import ElasticBit
+
+    c = BOLT
+    dense = _bolt_model(device)
+    g = torch.Generator(device=device).manual_seed(5)
+    ids = torch.randint(0, c["vocab"], (c["batch"], c["prefill"]), device=device, generator=g)
+    calib = torch.randint(0, c["vocab"], (2, 128), device=device, generator=g)
+    res = {}
+    d_pf, d_dec, d_out = _bolt_generate(dense, ids, device)
+    comp = ElasticBit.compress(copy.deepcopy(dense), calib, 0.01, backend="native")
+    bits = sorted({m.matrix.storageBits for m in comp.modules() if hasattr(m, "matrix")})
+    c_pf, c_dec, c_out = _bolt_generate(comp, ids, device)
+    with torch.inference_mode():  # closeness of the prefill logits to the dense model's
+        ld = dense(ids).float()
+        lc = comp(ids).float()
+        logits_rel = float((lc - ld).norm() / ld.norm())
+    for name, pf, dec in (("dense_fp16", d_pf, d_dec), ("elasticbit", c_pf, c_dec)):
+        res[name] = {"prefill_tok_s": round(c["batch"] * c["prefill"] / (pf * 1e-3), 1),
+                     "decode_tok_s": round(c["batch"] * c["steps"] / (dec * 1e-3), 1),
+                     "decode_ms_per_step": round(dec / c["steps"], 4)}
+    res["elasticbit"]["bits"] = bits
+    res["prefill_logits_rel_l2_vs_dense"] = round(logits_rel, 6)
+    # random-init logits are nearly flat, so greedy choices flip under small perturbations
+    res["greedy_tokens_equal_to_dense"] = round(float((c_out == d_out).float().mean()), 4)
+    res["workload"] = ("config4: BoltModel-shaped decoder (vocab 32000, dim 384, 12 q heads / 1 kv "
+                       "head, 6 layers, FFN 4x, tied FP16 head), N(0,0.02) init; batch 8, 512-token "
+                       "prefill of uniform random ids, 128 greedy steps (one CUDA graph per step); "
+                       "plain multi-query attention")
+    del dense, comp
+    torch.cuda.empty_cache()
+    return res
+
+
+# ---------------------------------------------------------------------------
 # CPU: the reference's `pytorch` route restated on the host cores
 # ---------------------------------------------------------------------------
 def cpu_baseline(seconds: float = 8.0, shape=(4096, 4096), bits: int = 10) -> dict:
@@ -770,11 +956,18 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-tp-stack", action="store_true")
+    ap.add_argument("--no-bolt", action="store_true", help="skip the config-4 decoder")
+    ap.add_argument("--bolt-only", action="store_true", help="run only the config-4 decoder")
     ap.add_argument("--nccl-only", action="store_true",
                     help="tp stack: all-reduce through NCCL even for M <= 16")
     args = ap.parse_args()
     if args.single:
         run_single(args)
+    elif args.bolt_only:
+        import torch
+
+        torch.cuda.set_device(0)
+        emit(run_bolt_decoder(torch.device("cuda", 0)))
     elif args.impl == "reference":
         run_reference(args)
     else:
