@@ -138,16 +138,47 @@ __global__ void materialize_kernel(const uint8_t* tiles, const float* scales, in
     const int64_t tile = id >> 5;
     const int64_t g = tile / kt, t = tile - (tile / kt) * kt;
     const uint8_t* base = tiles + tile * tile_bytes(B);
+    // the lane's words: 16-byte segments, then an 8- and a 4-byte one (word_offset)
     uint32_t w[B];
 #pragma unroll
-    for (int i = 0; i < B; ++i)
-        w[i] = *reinterpret_cast<const uint32_t*>(base + word_offset(B, lane, i));
+    for (int q = 0; q < B / 4; ++q) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(base + q * 512 + lane * 16));
+        w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
+    }
+    if constexpr ((B & 2) != 0) {
+        const uint2 v = __ldg(reinterpret_cast<const uint2*>(base + (B / 4) * 512 + lane * 8));
+        w[4 * (B / 4)] = v.x;
+        w[4 * (B / 4) + 1] = v.y;
+    }
+    if constexpr ((B & 1) != 0)
+        w[B - 1] = __ldg(reinterpret_cast<const uint32_t*>(base + (B / 4) * 512 + ((B & 2) ? 256 : 0) +
+                                                           lane * 4));
     const int r0 = int(g * kRowGroup) + (lane >> 2);
     const int kb = int(t * kKTile) + 16 * (lane & 3);
     uint32_t h[16];
     if constexpr (B == kFp16Bits) {
 #pragma unroll
         for (int p = 0; p < 16; ++p) h[p] = w[p];
+    } else if constexpr (B >= 8 && B <= 12) {
+        // paired f32x2 decode (the decode kernel's arithmetic)
+        const float sl = r0 < rows ? scales[r0] : 0.0f;
+        const float sh = r0 + 8 < rows ? scales[r0 + 8] : 0.0f;
+        PairConsts<B> pk;
+        pk.init(0x4B000000u);
+        const uint64_t s2[2] = {pack2f(sl, sl), pack2f(sh, sh)};
+        uint32_t lo[4], hi[4];
+        dequant_steps<B, 0>(w, pk, s2, lo, hi);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            h[r] = lo[r];
+            h[8 + r] = hi[r];
+        }
+        dequant_steps<B, 1>(w, pk, s2, lo, hi);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            h[4 + r] = lo[r];
+            h[12 + r] = hi[r];
+        }
     } else {
         const float sl = r0 < rows ? scales[r0] : 0.0f;
         const float sh = r0 + 8 < rows ? scales[r0 + 8] : 0.0f;
@@ -176,8 +207,9 @@ __global__ void materialize_kernel(const uint8_t* tiles, const float* scales, in
             reinterpret_cast<uint4*>(dst)[0] = make_uint4(v[0], v[1], v[2], v[3]);
             reinterpret_cast<uint4*>(dst)[1] = make_uint4(v[4], v[5], v[6], v[7]);
         } else {
-            for (int e = 0; e < 16 && kb + e < cols; ++e)
-                dst[e] = uint16_t(v[e >> 1] >> (16 * (e & 1)));
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+                if (kb + e < cols) dst[e] = uint16_t(v[e >> 1] >> (16 * (e & 1)));
         }
     }
 }
