@@ -904,13 +904,14 @@ def run_single(args) -> None:
         byts = sum(algorithmic_bytes(N, K, m.storageBits, M) for m in mats) / len(mats)
         out.update({"us_per_launch": round(us, 3), "GBps": round(byts / (us * 1e-6) / 1e9, 1),
                     "TFLOPs": round(2.0 * M * N * K / (us * 1e-6) / 1e12, 1)})
-        if nws:
-            # the materialise step alone (exact fp16 weight into the workspace)
+        if M > 256:
+            # the materialise step alone (exact fp16 weight into a buffer of its size)
+            w16 = torch.empty((N, K), dtype=torch.float16, device=device)
             gm = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gm):
                 for m in mats:
                     _ebx.check(lib.ebx_matrix_materialize(ctypes.c_void_p(m._native.handle),
-                                                          ws.data_ptr(), _ebx.stream_ptr()))
+                                                          w16.data_ptr(), _ebx.stream_ptr()))
             gm.replay()
             torch.cuda.synchronize()
             a.record()

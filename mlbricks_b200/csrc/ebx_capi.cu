@@ -349,9 +349,12 @@ ebx_status ebx_matrix_materialize(const ebx_matrix* h, void* dst, void* stream) 
 }
 
 uint64_t ebx_linear_workspace_bytes(const ebx_matrix* h, int64_t M) {
-    // M > kGemmMinRows: room for the exactly dequantised fp16 weight fed to the
-    // tensor-core GEMM; smaller M runs the decode kernel and needs nothing.
-    if (!h || M <= ebx::kGemmMinRows || (h->m.cols % 8) != 0) return 0;
+    // 16 < M <= 256: the decode-GEMM's fp32 split-K partials (when K is split);
+    // M > 256: room for the exactly dequantised fp16 weight fed to the tensor-core
+    // GEMM; M <= 16 runs the decode kernel and needs nothing.
+    if (!h || M <= ebx::kDgemmMinRows || (h->m.cols % 8) != 0) return 0;
+    if (M <= ebx::kDgemmMaxRows && ebx::dgemm_route(h->m, M)) return ebx::dgemm_workspace_bytes(h->m, M);
+    if (M <= ebx::kGemmMinRows) return 0;  // chunked decode
     return uint64_t(ebx::round_up(int64_t(h->m.rows) * h->m.cols * 2, 256));
 }
 
@@ -369,9 +372,23 @@ ebx_status ebx_linear(const ebx_matrix* h, const void* x, int64_t M, const void*
     DeviceGuard g(h->m.device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const uint64_t need = ebx_linear_workspace_bytes(h, M);
-    if (need > 0 && ebx::gemm_supported(h->m.cols, x, workspace)) {
+    if (M > ebx::kDgemmMinRows && M <= ebx::kDgemmMaxRows && ebx::dgemm_route(h->m, M) &&
+        ebx::dgemm_supported(h->m, M, x)) {
+        // weights decoded straight into tensor-core tiles (fp32 partials in the workspace
+        // when K is split over CTAs)
+        if (workspace_bytes < need || (need > 0 && !workspace)) {
+            set_error("ebx_linear: workspace missing or smaller than ebx_linear_workspace_bytes()");
+            return EBX_ERR_WORKSPACE;
+        }
+        EBX_CUDA(ebx::launch_dgemm(h->m, static_cast<const uint16_t*>(x), M,
+                                   static_cast<const uint16_t*>(bias), static_cast<uint16_t*>(y), y32,
+                                   workspace, workspace_bytes, s));
+        return EBX_OK;
+    }
+    if (M > ebx::kGemmMinRows && need > 0 && ebx::gemm_supported(h->m.cols, x, workspace)) {
         // prefill: exact fp16 weight into the workspace, then the tcgen05 GEMM
-        if (workspace_bytes < need) {
+        const uint64_t w16_bytes = uint64_t(ebx::round_up(int64_t(h->m.rows) * h->m.cols * 2, 256));
+        if (!workspace || workspace_bytes < w16_bytes) {
             set_error("ebx_linear: workspace missing or smaller than ebx_linear_workspace_bytes()");
             return EBX_ERR_WORKSPACE;
         }
@@ -417,11 +434,12 @@ ebx_status ebx_device_status(int32_t device, int32_t* status, int32_t clear) {
     }
     DeviceGuard g(device);
     if (!g.ok) return cuda_fail(cudaErrorInvalidDevice, "cudaSetDevice");
-    int v = 0, vg = 0, vx = 0;
+    int v = 0, vg = 0, vd = 0, vx = 0;
     EBX_CUDA(ebx::read_device_status(&v, clear != 0, nullptr));
     EBX_CUDA(ebx::read_gemm_status(&vg, clear != 0, nullptr));
+    EBX_CUDA(ebx::read_dgemm_status(&vd, clear != 0, nullptr));
     EBX_CUDA(ebx::read_xchg_status(&vx, clear != 0, nullptr));
-    *status = v ? v : (vg ? vg : vx);
+    *status = v ? v : (vg ? vg : (vd ? vd : vx));
     return EBX_OK;
 }
 

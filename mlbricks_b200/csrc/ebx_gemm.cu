@@ -327,6 +327,372 @@ bool make_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows)
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+
+// ---------------------------------------------------------------------------
+// Decode-GEMM for 16 < M <= 256 activation rows
+// ---------------------------------------------------------------------------
+// The weights are the 128-row side of tcgen05.mma (A operand) and the tokens
+// the N side (B operand, N = M rounded up to 16): a CTA owns 128 weight rows (8
+// row groups) and a contiguous range of k-blocks; the weights stream from HBM
+// once, as exact-width codes.  Per 64-k block:
+//   * warp 0 (one thread): one bulk copy per row group's supertile (b x 128
+//     bytes) and one TMA load of the activations' 64-k slice (M rows, 128-byte
+//     swizzle, rows past M filled with zeros) into a D-stage ring;
+//   * warps 2-5: decode two supertiles each to exact fp16 (the decode kernel's
+//     arithmetic) and store them, K-major with the 128-byte swizzle
+//     (16-byte chunk j of row n at n*128 + (j ^ (n & 7))*16), as the A tile;
+//     fence.proxy.async makes the stores visible to the tensor core;
+//   * warp 1 (one thread): four tcgen05.mma (K = 16) into a 128 x N fp32
+//     accumulator in TMEM, then tcgen05.commit frees the stage.
+// After the last k-block warps 2-5 read TMEM lanes 32(w % 4).. (one weight row
+// per thread) and write either y = fp16(acc (* s for integer codes) + bias)
+// directly, or, when K is split over S CTAs to fill the GPU, an fp32 partial
+// that dgemm_reduce_kernel adds in split order (deterministic).
+constexpr int kDgRows = 128;
+constexpr int kDgGroups = kDgRows / kRowGroup;  // 8 row groups per CTA
+constexpr int kDgThreads = 192;
+constexpr int kDgABytes = kDgRows * BK * 2;     // 16 KB decoded weight tile
+constexpr int kDgMaxTokens = 256;
+
+__device__ int g_dgemm_status = 0;
+
+struct DgArgs {
+    const uint8_t* tiles;
+    const float* scales;
+    const uint16_t* bias;
+    uint16_t* y;
+    float* y32;
+    float* part;  // [S][M][N] fp32 partials when S > 1
+    int M, N, kt, groups;
+    int S, kb_per;     // K splits and k-blocks per split
+    int stages, stage_bytes, mp, tmem_cols;
+    int b_off, c_off;  // byte offsets of the activation and code tiles in a stage
+};
+
+__device__ __forceinline__ bool dg_wait(uint32_t bar, uint32_t parity) {
+    if (mbar_wait_bounded(bar, parity)) return true;
+    atomicExch(&g_dgemm_status, 0x7104);
+    return false;
+}
+
+__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+                 : "memory");
+}
+
+// A-fragment registers of one lane's 32 codes (register 4s + rr: codes 2(4s+rr),
+// +1; rr odd -> row r0 + 8) -> exact fp16 pairs.
+template <int B, bool HW>
+__device__ __forceinline__ void dg_decode(const uint32_t (&w)[B], const uint64_t (&s2)[2], uint32_t (&af)[16]) {
+    if constexpr (B == kFp16Bits) {
+#pragma unroll
+        for (int p = 0; p < 16; ++p) af[p] = w[p];
+    } else if constexpr (HW) {
+        const float nb = -(8388608.0f + float(qmax_for(B)));
+        const uint64_t nb2 = pack2f(nb, nb);
+#pragma unroll
+        for (int p = 0; p < 16; ++p) af[p] = codes2_to_half(code_magic<B>(w, 2 * p), code_magic<B>(w, 2 * p + 1), nb2);
+    } else if constexpr (B >= 8 && B <= 12) {
+        PairConsts<B> pk;
+        pk.init(0x4B000000u);
+        uint32_t lo[4], hi[4];
+        dequant_steps<B, 0>(w, pk, s2, lo, hi);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            af[r] = lo[r];
+            af[8 + r] = hi[r];
+        }
+        dequant_steps<B, 1>(w, pk, s2, lo, hi);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            af[4 + r] = lo[r];
+            af[12 + r] = hi[r];
+        }
+    } else {
+        const float nb = -(8388608.0f + float(qmax_for(B)));
+        const uint64_t nb2 = pack2f(nb, nb);
+#pragma unroll
+        for (int p = 0; p < 16; ++p)
+            af[p] = dequant2(code_magic<B>(w, 2 * p), code_magic<B>(w, 2 * p + 1), nb2, s2[p & 1]);
+    }
+}
+
+template <int B, bool HW>
+__global__ void __launch_bounds__(kDgThreads, 1)
+    dgemm_kernel(const __grid_constant__ CUtensorMap tma_x, DgArgs a) {
+    constexpr int kCodeBytes = B * 128;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    const int D = a.stages;
+    const int SB = a.stage_bytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + D * SB);
+    uint64_t* ready = full + D;
+    uint64_t* empty = ready + D;
+    uint64_t* acc_full = empty + D;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int rb = blockIdx.x / a.S;
+    const int split = blockIdx.x % a.S;
+    const int kb0 = split * a.kb_per;
+    const int kb1 = min(a.kt, kb0 + a.kb_per);
+    const int nkb = kb1 - kb0;
+    const int g0 = rb * kDgGroups;
+    const int ngroups = min(kDgGroups, a.groups - g0);
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int i = 0; i < D; ++i) {
+                mbar_init(smem_u32(&full[i]), 1);
+                mbar_init(smem_u32(&ready[i]), 4);  // one arrival per decoding warp
+                mbar_init(smem_u32(&empty[i]), 1);
+            }
+            mbar_init(smem_u32(acc_full), 1);
+            fence_proxy_async_smem();
+        }
+        __syncwarp();
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(a.tmem_cols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {  // producer
+            for (int i = 0; i < nkb; ++i) {
+                const int st = i % D;
+                if (i >= D && !dg_wait(smem_u32(&empty[st]), uint32_t(((i / D) - 1) & 1))) break;
+                const int kb = kb0 + i;
+                const uint32_t bar = smem_u32(&full[st]);
+                uint8_t* stage = smem + st * SB;
+                mbar_expect_tx(bar, uint32_t(ngroups * kCodeBytes + a.mp * BK * 2));
+                tma_load_2d(smem_u32(stage + a.b_off), &tma_x, kb * BK, 0, bar);
+                for (int r = 0; r < ngroups; ++r)
+                    bulk_g2s(smem_u32(stage + a.c_off + r * kCodeBytes),
+                             a.tiles + (size_t(g0 + r) * a.kt + kb) * kCodeBytes, kCodeBytes, bar);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {  // MMA issuer
+            const uint32_t idesc = (1u << 4) | (uint32_t(a.mp >> 3) << 17) | (uint32_t(kDgRows >> 4) << 24);
+            bool ok = true;
+            for (int i = 0; i < nkb && ok; ++i) {
+                const int st = i % D;
+                const uint32_t ph = uint32_t(i / D) & 1u;
+                if (!dg_wait(smem_u32(&full[st]), ph) || !dg_wait(smem_u32(&ready[st]), ph)) {
+                    ok = false;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+                const uint32_t abase = smem_u32(smem + st * SB);
+                const uint32_t bbase = abase + uint32_t(a.b_off);
+#pragma unroll
+                for (int k = 0; k < BK / 16; ++k)
+                    umma_f16(tmem, sw128_desc(abase + k * 32), sw128_desc(bbase + k * 32), idesc,
+                             (i | k) != 0 ? 1u : 0u);
+                umma_commit(smem_u32(&empty[st]));
+            }
+            umma_commit(smem_u32(acc_full));  // fires when every MMA above has completed
+        }
+        __syncwarp();
+    } else {
+        // ---------------- decode (warps 2-5), then the epilogue ----------------
+        const int dw = warp - 2;
+        const int r0 = lane >> 2;
+        const int c = lane & 3;
+        uint64_t s2[2][2] = {{0, 0}, {0, 0}};
+        if constexpr (B != kFp16Bits && !HW) {
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int row = (g0 + 2 * dw + rr) * kRowGroup + r0 + 8 * h;
+                    const float sv = (2 * dw + rr < ngroups && row < a.N) ? a.scales[row] : 0.0f;
+                    s2[rr][h] = pack2f(sv, sv);
+                }
+        }
+        for (int i = 0; i < nkb; ++i) {
+            const int st = i % D;
+            if (!dg_wait(smem_u32(&full[st]), uint32_t(i / D) & 1u)) break;
+            const uint8_t* stage = smem + st * SB;
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+                const int r = 2 * dw + rr;
+                if (r >= ngroups) continue;  // rows past N: never read back
+                const uint8_t* cb = stage + a.c_off + r * kCodeBytes;
+                uint32_t w[B];
+#pragma unroll
+                for (int q = 0; q < B / 4; ++q) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(cb + q * 512 + lane * 16);
+                    w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
+                }
+                if constexpr ((B & 2) != 0) {
+                    const uint2 v = *reinterpret_cast<const uint2*>(cb + (B / 4) * 512 + lane * 8);
+                    w[4 * (B / 4)] = v.x;
+                    w[4 * (B / 4) + 1] = v.y;
+                }
+                if constexpr ((B & 1) != 0)
+                    w[B - 1] = *reinterpret_cast<const uint32_t*>(cb + (B / 4) * 512 + ((B & 2) ? 256 : 0) +
+                                                                  lane * 4);
+                uint32_t af[16];
+                dg_decode<B, HW>(w, s2[rr], af);
+                // rows 16r + r0 (+8) of the A tile, k = 16c..16c+15: chunks 2c, 2c+1
+                const uint32_t abase = smem_u32(stage);
+                const int nlo = 16 * r + r0, nhi = nlo + 8;
+                auto chunk = [&](int n, int j) {
+                    return abase + uint32_t(n * 128 + ((j ^ (n & 7)) << 4));
+                };
+                sts128(chunk(nlo, 2 * c), af[0], af[2], af[4], af[6]);
+                sts128(chunk(nlo, 2 * c + 1), af[8], af[10], af[12], af[14]);
+                sts128(chunk(nhi, 2 * c), af[1], af[3], af[5], af[7]);
+                sts128(chunk(nhi, 2 * c + 1), af[9], af[11], af[13], af[15]);
+            }
+            fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&ready[st]));
+        }
+        // epilogue: TMEM lane = weight row, column = token
+        if (dg_wait(smem_u32(acc_full), 0u)) {
+            asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+            const int quarter = warp & 3;
+            const int row = rb * kDgRows + quarter * 32 + lane;
+            float sc = 1.0f, bv = 0.0f;
+            if (row < a.N) {
+                if constexpr (HW && B != kFp16Bits) sc = a.scales[row];
+                if (a.bias && a.S == 1) bv = __half2float(__ushort_as_half(a.bias[row]));
+            }
+#pragma unroll 1
+            for (int t0 = 0; t0 < a.mp; t0 += 16) {
+                uint32_t v[16];
+                const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + uint32_t(t0);
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+                    "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+                    : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
+                      "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]),
+                      "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+                    : "r"(taddr));
+                asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+                if (row >= a.N) continue;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int tok = t0 + j;
+                    if (tok >= a.M) break;
+                    float f = __uint_as_float(v[j]);
+                    if (a.S == 1) {
+                        f = f * sc + bv;
+                        a.y[size_t(tok) * a.N + row] = __half_as_ushort(__float2half_rn(f));
+                        if (a.y32) a.y32[size_t(tok) * a.N + row] = f;
+                    } else {
+                        a.part[(size_t(split) * a.M + tok) * a.N + row] = f;
+                    }
+                }
+            }
+        }
+    }
+
+    asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem),
+                     "r"(a.tmem_cols)
+                     : "memory");
+    }
+}
+
+// y = fp16(sum over splits in order (* s for integer codes) + bias); four outputs per
+// thread (N % 4 == 0) or one.
+template <bool HW>
+__global__ void dgemm_reduce_kernel(const float* part, int S, int M, int N, const float* scales,
+                                    const uint16_t* bias, uint16_t* y, float* y32) {
+    const size_t total = size_t(M) * size_t(N);
+    const bool vec = (N & 3) == 0;
+    const size_t i0 = (size_t(blockIdx.x) * blockDim.x + threadIdx.x) * (vec ? 4 : 1);
+    if (i0 >= total) return;
+    const int row0 = int(i0 % uint32_t(N));
+    if (vec) {
+        float4 v = *reinterpret_cast<const float4*>(part + i0);
+        for (int s = 1; s < S; ++s) {
+            const float4 u = *reinterpret_cast<const float4*>(part + size_t(s) * total + i0);
+            v.x += u.x; v.y += u.y; v.z += u.z; v.w += u.w;
+        }
+        float f[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if constexpr (HW) f[j] *= scales[row0 + j];
+            if (bias) f[j] += __half2float(__ushort_as_half(bias[row0 + j]));
+        }
+        uint2 h;
+        h.x = pack_half2(f[0], f[1]);
+        h.y = pack_half2(f[2], f[3]);
+        *reinterpret_cast<uint2*>(y + i0) = h;
+        if (y32) *reinterpret_cast<float4*>(y32 + i0) = make_float4(f[0], f[1], f[2], f[3]);
+        return;
+    }
+    float v = part[i0];
+    for (int s = 1; s < S; ++s) v += part[size_t(s) * total + i0];
+    if constexpr (HW) v *= scales[row0];
+    if (bias) v += __half2float(__ushort_as_half(bias[row0]));
+    y[i0] = __half_as_ushort(__float2half_rn(v));
+    if (y32) y32[i0] = v;
+}
+
+struct DgPlan {
+    int S, kb_per, mp, tmem_cols, stages, stage_bytes, b_off, c_off, smem;
+};
+
+DgPlan dg_plan(const Matrix& m, int64_t M, int sms) {
+    DgPlan p{};
+    p.mp = int(round_up(M, 16));
+    p.tmem_cols = p.mp <= 32 ? 32 : (p.mp <= 64 ? 64 : (p.mp <= 128 ? 128 : 256));
+    const int kt = int(m.kt);
+    const int rbs = int((m.groups + kDgGroups - 1) / kDgGroups);
+    // split K until the grid covers most SMs, keeping >= 4 k-blocks per split
+    int S = 1;
+    while (S < 16 && int64_t(rbs) * S * 5 < int64_t(sms) * 4 && kt / (2 * S) >= 4) S *= 2;
+    p.S = S;
+    p.kb_per = (kt + S - 1) / S;
+    p.S = (kt + p.kb_per - 1) / p.kb_per;  // no empty split
+    const int bbytes = p.mp * BK * 2;
+    const int cbytes = kDgGroups * (m.bits == 16 ? 2048 : m.bits * 128);
+    p.b_off = kDgABytes;
+    p.c_off = p.b_off + bbytes;
+    p.stage_bytes = int(round_up(p.c_off + cbytes, 1024));
+    const int budget = 227 * 1024 - 1024 - 256;
+    int D = budget / p.stage_bytes;
+    p.stages = D > 6 ? 6 : D;
+    p.smem = p.stages * p.stage_bytes + 1024 + 256;
+    return p;
+}
+
+template <int B, bool HW>
+cudaError_t launch_dgemm_b(const Matrix& m, const CUtensorMap& tx, const DgArgs& a, unsigned grid,
+                           int smem, int dev, cudaStream_t s) {
+    auto kern = dgemm_kernel<B, HW>;
+    static std::atomic<uint64_t> configured{0};
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(configured.load(std::memory_order_relaxed) & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e != cudaSuccess) return e;
+        configured.fetch_or(bit);
+    }
+    kern<<<grid, kDgThreads, smem, s>>>(tx, a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || a.S == 1) return e;
+    const int64_t total = int64_t(a.M) * a.N;
+    const int64_t threads = (a.N % 4) == 0 ? total / 4 : total;
+    dgemm_reduce_kernel<HW && B != kFp16Bits><<<unsigned((threads + 255) / 256), 256, 0, s>>>(
+        a.part, a.S, a.M, a.N, m.scales, a.bias, a.y, a.y32);
+    return cudaGetLastError();
+}
 }  // namespace
 
 cudaError_t read_gemm_status(int* status, bool clear, cudaStream_t s) {
@@ -395,6 +761,92 @@ cudaError_t launch_gemm_f16(const uint16_t* x, const uint16_t* w16, int64_t M, i
     if (c256 <= c128 && c256 <= c64) return launch_gemm_bn<256>(x, w16, M, N, K, bias, y, y32, sms, dev, s);
     if (c128 <= c64) return launch_gemm_bn<128>(x, w16, M, N, K, bias, y, y32, sms, dev, s);
     return launch_gemm_bn<64>(x, w16, M, N, K, bias, y, y32, sms, dev, s);
+}
+
+int gemm_sm_count(int dev) {
+    static std::atomic<int> cache[64];
+    int sms = cache[dev & 63].load(std::memory_order_relaxed);
+    if (sms == 0) {
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+        cache[dev & 63].store(sms, std::memory_order_relaxed);
+    }
+    return sms;
+}
+
+// Measured on the BASELINE shapes: the decode-GEMM beats chunked decode for every
+// 16 < M <= 128 and materialise + GEMM for M <= 128 and, up to 256 rows, when K >= 8192
+// (14336x4096 at M = 256: 64 vs 104 us); with K = 4096 and 128 < M <= 256 the separate
+// materialise + GEMM is as fast or faster.
+bool dgemm_supported(const Matrix& m, int64_t M, const void* x) {
+    return dgemm_route(m, M) && M <= kDgMaxTokens && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+           encode_fn() != nullptr;
+}
+
+uint64_t dgemm_workspace_bytes(const Matrix& m, int64_t M) {
+    const DgPlan p = dg_plan(m, M, gemm_sm_count(m.device));
+    return p.S > 1 ? uint64_t(round_up(int64_t(p.S) * M * m.rows * 4, 256)) : 0;
+}
+
+cudaError_t launch_dgemm(const Matrix& m, const uint16_t* x, int64_t M, const uint16_t* bias,
+                         uint16_t* y, float* y32, void* ws, uint64_t ws_bytes, cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const DgPlan p = dg_plan(m, M, gemm_sm_count(dev));
+    if (p.stages < 2) return cudaErrorInvalidConfiguration;
+    if (p.S > 1 && (ws == nullptr || ws_bytes < dgemm_workspace_bytes(m, M))) return cudaErrorInvalidValue;
+    CUtensorMap tx;
+    if (!make_map(&tx, x, int(M), m.cols, p.mp)) return cudaErrorInvalidValue;
+    DgArgs a{};
+    a.tiles = m.tiles;
+    a.scales = m.scales;
+    a.bias = bias;
+    a.y = y;
+    a.y32 = y32;
+    a.part = static_cast<float*>(ws);
+    a.M = int(M);
+    a.N = m.rows;
+    a.kt = int(m.kt);
+    a.groups = int(m.groups);
+    a.S = p.S;
+    a.kb_per = p.kb_per;
+    a.stages = p.stages;
+    a.stage_bytes = p.stage_bytes;
+    a.mp = p.mp;
+    a.tmem_cols = p.tmem_cols;
+    a.b_off = p.b_off;
+    a.c_off = p.c_off;
+    const unsigned grid = unsigned(((m.groups + kDgGroups - 1) / kDgGroups) * p.S);
+    const bool hw = m.exec_width < 16 && m.bits <= 8;
+    switch (m.bits) {
+#define EBX_DG_CASE(BB)                                                                  \
+    case BB:                                                                             \
+        return hw ? launch_dgemm_b<BB, true>(m, tx, a, grid, p.smem, dev, s)             \
+                  : launch_dgemm_b<BB, false>(m, tx, a, grid, p.smem, dev, s);
+        EBX_DG_CASE(3) EBX_DG_CASE(4) EBX_DG_CASE(5) EBX_DG_CASE(6) EBX_DG_CASE(7) EBX_DG_CASE(8)
+#undef EBX_DG_CASE
+#define EBX_DG_CASE(BB) \
+    case BB:            \
+        return launch_dgemm_b<BB, false>(m, tx, a, grid, p.smem, dev, s);
+        EBX_DG_CASE(9) EBX_DG_CASE(10) EBX_DG_CASE(11) EBX_DG_CASE(12) EBX_DG_CASE(13)
+        EBX_DG_CASE(14) EBX_DG_CASE(15) EBX_DG_CASE(16)
+#undef EBX_DG_CASE
+        default:
+            return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t read_dgemm_status(int* status, bool clear, cudaStream_t s) {
+    cudaError_t e = cudaMemcpyFromSymbolAsync(status, g_dgemm_status, sizeof(int), 0,
+                                              cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e == cudaSuccess && clear) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbolAsync(g_dgemm_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    }
+    return e;
 }
 
 }  // namespace ebx

@@ -85,6 +85,21 @@ bool gemm_supported(int K, const void* x, const void* w16);
 cudaError_t launch_gemm_f16(const uint16_t* x, const uint16_t* w16, int64_t M, int N, int K,
                             const uint16_t* bias, uint16_t* y, float* y32, cudaStream_t s);
 cudaError_t read_gemm_status(int* status, bool clear, cudaStream_t s);
+// Decode-GEMM for 16 < M <= 256: codes decoded straight into tcgen05 tiles (weights as the
+// 128-row MMA side, tokens as N); K split over CTAs when needed, with an fp32 partial
+// workspace of dgemm_workspace_bytes() reduced in split order.
+constexpr int64_t kDgemmMinRows = 16;
+constexpr int64_t kDgemmMaxRows = 256;
+// dgemm_route: the shape rule alone (16 < M <= 128, or M <= 256 with K >= 8192), which
+// also decides ebx_linear_workspace_bytes; dgemm_supported adds the activation checks.
+inline bool dgemm_route(const Matrix& m, int64_t M) {
+    return M > kDgemmMinRows && M <= kDgemmMaxRows && (M <= 128 || m.kt >= 128) && (m.cols % 8) == 0;
+}
+bool dgemm_supported(const Matrix& m, int64_t M, const void* x);
+uint64_t dgemm_workspace_bytes(const Matrix& m, int64_t M);
+cudaError_t launch_dgemm(const Matrix& m, const uint16_t* x, int64_t M, const uint16_t* bias,
+                         uint16_t* y, float* y32, void* ws, uint64_t ws_bytes, cudaStream_t s);
+cudaError_t read_dgemm_status(int* status, bool clear, cudaStream_t s);
 
 // ebx_analyze.cu ------------------------------------------------------------
 cudaError_t launch_analyze(const float* w, int rows, int cols, const float* x, int samples,

@@ -1,4 +1,5 @@
-"""Decode (M <= 16 per launch) at BASELINE sizes and ragged shapes, through the C ABI.
+"""Decode (M <= 16 per launch) and the decode-GEMM (16 < M <= 256) at BASELINE sizes and
+ragged shapes, through the C ABI.
 
 Covers the 4096x4096, 14336x4096 and 4096x14336 decode shapes and ragged ones
 (N not a multiple of 16, one or two k-tiles per row) at every bit-width class
@@ -180,3 +181,94 @@ def test_decode_graph_replay_matches_eager(lib):
     st = ctypes.c_int32(-1)
     _ebx.check(lib.ebx_device_status(0, ctypes.byref(st), 0))
     assert st.value == 0
+
+
+# ---------------------------------------------------------------------------
+# 16 < M <= 256: the decode-GEMM (codes decoded straight into tensor-core tiles)
+# ---------------------------------------------------------------------------
+def run_ws(lib, h, x, rows, bias=None):
+    """ebx_linear with the workspace ebx_linear_workspace_bytes asks for."""
+    M = x.shape[0]
+    y = torch.empty((M, rows), dtype=torch.float16, device=dev())
+    y32 = torch.empty((M, rows), dtype=torch.float32, device=dev())
+    nws = int(lib.ebx_linear_workspace_bytes(h.h, M))
+    ws = torch.empty(max(nws, 1), dtype=torch.uint8, device=dev())
+    _ebx.check(lib.ebx_linear(h.h, x.data_ptr(), M, None if bias is None else bias.data_ptr(),
+                              y.data_ptr(), y32.data_ptr(), ws.data_ptr(), nws, _ebx.stream_ptr()))
+    return y, y32
+
+
+DG_SHAPES = [
+    (4096, 4096, 10),   # K split over CTAs (32 weight-row blocks)
+    (14336, 4096, 9),   # 112 row blocks
+    (4096, 14336, 11),  # K = 14336
+    (1000, 576, 12),    # ragged rows, 9 k-tiles
+    (200, 72, 13),      # K not a multiple of 64 (activations past K read as zeros)
+]
+
+
+@pytest.mark.parametrize("rows,cols,bits", DG_SHAPES)
+@pytest.mark.parametrize("M", [17, 33, 64, 100, 256])
+def test_decode_gemm_full_semantics(lib, rows, cols, bits, M):
+    h, q, s = make(lib, rows, cols, bits, seed=rows + cols + bits + M)
+    w16 = materialize(lib, h, rows, cols)
+    x = torch.randn((M, cols), device=dev()).half()
+    bias = (0.1 * torch.randn(rows, device=dev())).half()
+    y, y32 = run_ws(lib, h, x, rows, bias)
+    torch.cuda.synchronize()
+    check(y, y32, x.double() @ w16.double().t() + bias.double())
+    st = ctypes.c_int32(-1)
+    _ebx.check(lib.ebx_device_status(0, ctypes.byref(st), 0))
+    assert st.value == 0
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("M", [24, 128])
+def test_decode_gemm_integer_semantics(lib, bits, M):
+    rows, cols = 3000, 1024
+    h, q, s = make(lib, rows, cols, bits, seed=bits + M)
+    _ebx.check(lib.ebx_matrix_set_execution_width(h.h, 8))
+    x = torch.randn((M, cols), device=dev()).half()
+    y, y32 = run_ws(lib, h, x, rows)
+    torch.cuda.synchronize()
+    check(y, y32, (x.double() @ q.double().t()) * s.double())
+
+
+def test_decode_gemm_fp16_storage(lib):
+    rows, cols, M = 640, 512, 48
+    w = (0.02 * torch.randn((rows, cols), device=dev())).half().contiguous()
+    hp = ctypes.c_void_p()
+    _ebx.check(lib.ebx_matrix_create_from_fp16(w.data_ptr(), rows, cols, 0, _ebx.stream_ptr(),
+                                               ctypes.byref(hp)))
+    h = Handle(hp.value)
+    x = torch.randn((M, cols), device=dev()).half()
+    y, y32 = run_ws(lib, h, x, rows)
+    torch.cuda.synchronize()
+    check(y, y32, x.double() @ w.double().t())
+
+
+def test_decode_gemm_graph_replay_and_repeats(lib):
+    rows, cols, bits = 4096, 4096, 10
+    h, q, s = make(lib, rows, cols, bits, seed=77)
+    outs = []
+    for M in (64, 200, 64):
+        x = torch.randn((M, cols), device=dev(), generator=torch.Generator(device=dev()).manual_seed(M)).half()
+        outs.append(run_ws(lib, h, x, rows)[1].clone())
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[2])
+    M = 96
+    x = torch.randn((M, cols), device=dev()).half()
+    eager = run_ws(lib, h, x, rows)[1].clone()
+    nws = int(lib.ebx_linear_workspace_bytes(h.h, M))
+    ws = torch.empty(max(nws, 1), dtype=torch.uint8, device=dev())
+    y = torch.empty((M, rows), dtype=torch.float16, device=dev())
+    y32 = torch.empty((M, rows), dtype=torch.float32, device=dev())
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(dev())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        _ebx.check(lib.ebx_linear(h.h, x.data_ptr(), M, None, y.data_ptr(), y32.data_ptr(),
+                                  ws.data_ptr(), nws, _ebx.stream_ptr()))
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(eager, y32)

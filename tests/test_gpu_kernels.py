@@ -326,13 +326,15 @@ def test_device_status_healthy_after_all_kernels(lib):
                                          (256, 1536, 384), (512, 4096, 4096), (200, 4096, 14336),
                                          (1024, 4096, 512), (2048, 4096, 256), (2100, 2600, 200)])
 def test_prefill_gemm(lib, M, rows, cols):
-    """M > 64: exact fp16 weight materialised into the workspace, tcgen05 GEMM."""
+    """M > 256: exact fp16 weight materialised into the workspace, tcgen05 GEMM;
+    16 < M <= 256: the decode-GEMM (codes decoded into tensor-core tiles)."""
     bits = 10
     w = O.baseline_weights(rows, cols, seed=M + rows)
     s = O.row_scales(w, bits)
     q = O.quantize(w, s, bits)
     h = from_codes(lib, q, s, bits)
-    assert lib.ebx_linear_workspace_bytes(h.h, M) >= rows * cols * 2
+    if M > 256:
+        assert lib.ebx_linear_workspace_bytes(h.h, M) >= rows * cols * 2
     x = O.normal((M, cols), seed=M).astype(np.float16)
     bias = O.normal((rows,), seed=5, scale=0.1).astype(np.float16)
     y16, y32 = linear(lib, h, x, rows, bias)
@@ -346,7 +348,15 @@ def test_prefill_gemm(lib, M, rows, cols):
 def test_prefill_without_workspace_is_refused(lib):
     q, s = random_codes(64, 128, 9, seed=2)
     h = from_codes(lib, q, s, 9)
-    x = torch.zeros((100, 128), dtype=torch.float16, device=dev())
-    y = torch.empty((100, 64), dtype=torch.float16, device=dev())
+    x = torch.zeros((300, 128), dtype=torch.float16, device=dev())
+    y = torch.empty((300, 64), dtype=torch.float16, device=dev())
+    st = lib.ebx_linear(h.h, x.data_ptr(), 300, None, y.data_ptr(), None, None, 0, stream())
+    assert st == _ebx.EBX_ERR_WORKSPACE
+    # decode-GEMM with K split over CTAs: the fp32 partials need the workspace too
+    q, s = random_codes(512, 4096, 9, seed=3)
+    h = from_codes(lib, q, s, 9)
+    assert lib.ebx_linear_workspace_bytes(h.h, 100) > 0
+    x = torch.zeros((100, 4096), dtype=torch.float16, device=dev())
+    y = torch.empty((100, 512), dtype=torch.float16, device=dev())
     st = lib.ebx_linear(h.h, x.data_ptr(), 100, None, y.data_ptr(), None, None, 0, stream())
     assert st == _ebx.EBX_ERR_WORKSPACE
