@@ -24,6 +24,8 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <cmath>
+#include <cstdlib>
 #include <mutex>
 
 #include "ebx_common.cuh"
@@ -338,19 +340,20 @@ bool make_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows)
 //   * warp 0 (one thread): one bulk copy per row group's supertile (b x 128
 //     bytes) and one TMA load of the activations' 64-k slice (M rows, 128-byte
 //     swizzle, rows past M filled with zeros) into a D-stage ring;
-//   * warps 2-5: decode two supertiles each to exact fp16 (the decode kernel's
-//     arithmetic) and store them, K-major with the 128-byte swizzle
+//   * warps 2-9: decode one supertile each to exact fp16 (the decode kernel's
+//     arithmetic) and store it, K-major with the 128-byte swizzle
 //     (16-byte chunk j of row n at n*128 + (j ^ (n & 7))*16), as the A tile;
 //     fence.proxy.async makes the stores visible to the tensor core;
 //   * warp 1 (one thread): four tcgen05.mma (K = 16) into a 128 x N fp32
 //     accumulator in TMEM, then tcgen05.commit frees the stage.
-// After the last k-block warps 2-5 read TMEM lanes 32(w % 4).. (one weight row
-// per thread) and write either y = fp16(acc (* s for integer codes) + bias)
+// After the last k-block warps 2-9 read TMEM lanes 32(w % 4).. (one weight row
+// per thread; two warps per lane quarter take alternate 16-token chunks) and write either y = fp16(acc (* s for integer codes) + bias)
 // directly, or, when K is split over S CTAs to fill the GPU, an fp32 partial
 // that dgemm_reduce_kernel adds in split order (deterministic).
 constexpr int kDgRows = 128;
 constexpr int kDgGroups = kDgRows / kRowGroup;  // 8 row groups per CTA
-constexpr int kDgThreads = 192;
+constexpr int kDgDecoders = 8;                   // one decoding warp per row group
+constexpr int kDgThreads = 64 + 32 * kDgDecoders;  // producer, MMA issuer, decoders
 constexpr int kDgABytes = kDgRows * BK * 2;     // 16 KB decoded weight tile
 constexpr int kDgMaxTokens = 256;
 
@@ -418,7 +421,7 @@ __device__ __forceinline__ void dg_decode(const uint32_t (&w)[B], const uint64_t
 }
 
 template <int B, bool HW>
-__global__ void __launch_bounds__(kDgThreads, 1)
+__global__ void __launch_bounds__(kDgThreads, 2)
     dgemm_kernel(const __grid_constant__ CUtensorMap tma_x, DgArgs a) {
     constexpr int kCodeBytes = B * 128;
     extern __shared__ uint8_t smem_raw[];
@@ -445,7 +448,7 @@ __global__ void __launch_bounds__(kDgThreads, 1)
         if (lane == 0) {
             for (int i = 0; i < D; ++i) {
                 mbar_init(smem_u32(&full[i]), 1);
-                mbar_init(smem_u32(&ready[i]), 4);  // one arrival per decoding warp
+                mbar_init(smem_u32(&ready[i]), kDgDecoders);  // one arrival per decoding warp
                 mbar_init(smem_u32(&empty[i]), 1);
             }
             mbar_init(smem_u32(acc_full), 1);
@@ -464,19 +467,24 @@ __global__ void __launch_bounds__(kDgThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
-        if (lane == 0) {  // producer
-            for (int i = 0; i < nkb; ++i) {
-                const int st = i % D;
-                if (i >= D && !dg_wait(smem_u32(&empty[st]), uint32_t(((i / D) - 1) & 1))) break;
-                const int kb = kb0 + i;
-                const uint32_t bar = smem_u32(&full[st]);
-                uint8_t* stage = smem + st * SB;
+        // producer: lane 0 arms the stage and loads the activations, lanes r < ngroups
+        // copy row group r's supertile (the copies are issued in parallel)
+        for (int i = 0; i < nkb; ++i) {
+            const int st = i % D;
+            bool ok = true;
+            if (lane == 0 && i >= D) ok = dg_wait(smem_u32(&empty[st]), uint32_t(((i / D) - 1) & 1));
+            if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+            const int kb = kb0 + i;
+            const uint32_t bar = smem_u32(&full[st]);
+            uint8_t* stage = smem + st * SB;
+            if (lane == 0) {
                 mbar_expect_tx(bar, uint32_t(ngroups * kCodeBytes + a.mp * BK * 2));
                 tma_load_2d(smem_u32(stage + a.b_off), &tma_x, kb * BK, 0, bar);
-                for (int r = 0; r < ngroups; ++r)
-                    bulk_g2s(smem_u32(stage + a.c_off + r * kCodeBytes),
-                             a.tiles + (size_t(g0 + r) * a.kt + kb) * kCodeBytes, kCodeBytes, bar);
             }
+            __syncwarp();
+            if (lane < ngroups)
+                bulk_g2s(smem_u32(stage + a.c_off + lane * kCodeBytes),
+                         a.tiles + (size_t(g0 + lane) * a.kt + kb) * kCodeBytes, kCodeBytes, bar);
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -503,29 +511,24 @@ __global__ void __launch_bounds__(kDgThreads, 1)
         }
         __syncwarp();
     } else {
-        // ---------------- decode (warps 2-5), then the epilogue ----------------
-        const int dw = warp - 2;
+        // ---------------- decode (warps 2-9), then the epilogue ----------------
+        const int r = warp - 2;  // this warp's row group within the CTA
         const int r0 = lane >> 2;
         const int c = lane & 3;
-        uint64_t s2[2][2] = {{0, 0}, {0, 0}};
+        uint64_t s2[2] = {0, 0};
         if constexpr (B != kFp16Bits && !HW) {
 #pragma unroll
-            for (int rr = 0; rr < 2; ++rr)
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int row = (g0 + 2 * dw + rr) * kRowGroup + r0 + 8 * h;
-                    const float sv = (2 * dw + rr < ngroups && row < a.N) ? a.scales[row] : 0.0f;
-                    s2[rr][h] = pack2f(sv, sv);
-                }
+            for (int h = 0; h < 2; ++h) {
+                const int row = (g0 + r) * kRowGroup + r0 + 8 * h;
+                const float sv = (r < ngroups && row < a.N) ? a.scales[row] : 0.0f;
+                s2[h] = pack2f(sv, sv);
+            }
         }
         for (int i = 0; i < nkb; ++i) {
             const int st = i % D;
             if (!dg_wait(smem_u32(&full[st]), uint32_t(i / D) & 1u)) break;
             const uint8_t* stage = smem + st * SB;
-#pragma unroll
-            for (int rr = 0; rr < 2; ++rr) {
-                const int r = 2 * dw + rr;
-                if (r >= ngroups) continue;  // rows past N: never read back
+            if (r < ngroups) {  // rows past N: never read back
                 const uint8_t* cb = stage + a.c_off + r * kCodeBytes;
                 uint32_t w[B];
 #pragma unroll
@@ -542,7 +545,7 @@ __global__ void __launch_bounds__(kDgThreads, 1)
                     w[B - 1] = *reinterpret_cast<const uint32_t*>(cb + (B / 4) * 512 + ((B & 2) ? 256 : 0) +
                                                                   lane * 4);
                 uint32_t af[16];
-                dg_decode<B, HW>(w, s2[rr], af);
+                dg_decode<B, HW>(w, s2, af);
                 // rows 16r + r0 (+8) of the A tile, k = 16c..16c+15: chunks 2c, 2c+1
                 const uint32_t abase = smem_u32(stage);
                 const int nlo = 16 * r + r0, nhi = nlo + 8;
@@ -568,8 +571,9 @@ __global__ void __launch_bounds__(kDgThreads, 1)
                 if constexpr (HW && B != kFp16Bits) sc = a.scales[row];
                 if (a.bias && a.S == 1) bv = __half2float(__ushort_as_half(a.bias[row]));
             }
+            const int half = (warp - 2) >> 2;  // two warps per lane quarter: alternate chunks
 #pragma unroll 1
-            for (int t0 = 0; t0 < a.mp; t0 += 16) {
+            for (int t0 = 16 * half; t0 < a.mp; t0 += 32) {
                 uint32_t v[16];
                 const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + uint32_t(t0);
                 asm volatile(
@@ -655,21 +659,48 @@ DgPlan dg_plan(const Matrix& m, int64_t M, int sms) {
     p.tmem_cols = p.mp <= 32 ? 32 : (p.mp <= 64 ? 64 : (p.mp <= 128 ? 128 : 256));
     const int kt = int(m.kt);
     const int rbs = int((m.groups + kDgGroups - 1) / kDgGroups);
-    // split K until the grid covers most SMs, keeping >= 4 k-blocks per split
-    int S = 1;
-    while (S < 16 && int64_t(rbs) * S * 5 < int64_t(sms) * 4 && kt / (2 * S) >= 4) S *= 2;
-    p.S = S;
-    p.kb_per = (kt + S - 1) / S;
-    p.S = (kt + p.kb_per - 1) / p.kb_per;  // no empty split
     const int bbytes = p.mp * BK * 2;
     const int cbytes = kDgGroups * (m.bits == 16 ? 2048 : m.bits * 128);
     p.b_off = kDgABytes;
     p.c_off = p.b_off + bbytes;
     p.stage_bytes = int(round_up(p.c_off + cbytes, 1024));
-    const int budget = 227 * 1024 - 1024 - 256;
-    int D = budget / p.stage_bytes;
-    p.stages = D > 6 ? 6 : D;
-    p.smem = p.stages * p.stage_bytes + 1024 + 256;
+    // Two CTAs per SM when each can still hold a ring of two or three stages
+    // (measured: more stages at one CTA per SM do not help), else one CTA with up to six.
+    constexpr int kOverhead = 1024 + 256;
+    static const int cap_env = [] {  // EBX_DG_STAGES=n caps the ring depth (measurement knob)
+        const char* e = std::getenv("EBX_DG_STAGES");
+        const int v = e ? std::atoi(e) : 0;
+        return v >= 2 && v <= 12 ? v : 0;
+    }();
+    int per_sm = 1;
+    int D = (227 * 1024 - kOverhead) / p.stage_bytes;
+    D = D > 6 ? 6 : D;
+    const int D2 = (227 * 1024 / 2 - kOverhead) / p.stage_bytes;
+    if (D2 >= 2) {
+        per_sm = 2;
+        D = D2 > 3 ? 3 : D2;
+    }
+    if (cap_env && D > cap_env) D = cap_env;
+    p.stages = D;
+    p.smem = D * p.stage_bytes + kOverhead;
+    // K split: minimise (waves x k-blocks per split) x ~0.5 us + the fp32 partials'
+    // write and read (S * M * N * 8 bytes at ~5 TB/s); at least 4 k-blocks per split
+    const double slots = double(per_sm) * sms;
+    double best = 1e30;
+    int bestS = 1;
+    for (int S = 1; S <= 16 && (S == 1 || kt / S >= 4); S *= 2) {
+        const int kb_per = (kt + S - 1) / S;
+        const int splits = (kt + kb_per - 1) / kb_per;
+        const double waves = std::ceil(double(rbs) * splits / slots);
+        const double t = waves * kb_per * 0.5 +
+                         (splits > 1 ? double(splits) * double(M) * m.rows * 8.0 / 5.0e6 : 0.0);
+        if (t < best - 1e-9) {
+            best = t;
+            bestS = splits;
+        }
+    }
+    p.kb_per = (kt + bestS - 1) / bestS;
+    p.S = (kt + p.kb_per - 1) / p.kb_per;  // no empty split
     return p;
 }
 
