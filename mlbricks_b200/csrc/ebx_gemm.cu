@@ -561,6 +561,9 @@ __global__ void __launch_bounds__(kDgThreads, 2)
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&ready[st]));
         }
+        // the split-K reduction (or the next layer) may be scheduled now; it waits for
+        // this grid to complete before it reads anything this grid writes
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
         // epilogue: TMEM lane = weight row, column = token
         if (dg_wait(smem_u32(acc_full), 0u)) {
             asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
@@ -617,6 +620,9 @@ __global__ void __launch_bounds__(kDgThreads, 2)
 template <bool HW>
 __global__ void dgemm_reduce_kernel(const float* part, int S, int M, int N, const float* scales,
                                     const uint16_t* bias, uint16_t* y, float* y32) {
+    // launched with programmatic dependent launch: the partials are read only once the
+    // decode-GEMM grid has completed (a no-op wait when launched without it)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const size_t total = size_t(M) * size_t(N);
     const bool vec = (N & 3) == 0;
     const size_t i0 = (size_t(blockIdx.x) * blockDim.x + threadIdx.x) * (vec ? 4 : 1);
@@ -720,9 +726,17 @@ cudaError_t launch_dgemm_b(const Matrix& m, const CUtensorMap& tx, const DgArgs&
     if (e != cudaSuccess || a.S == 1) return e;
     const int64_t total = int64_t(a.M) * a.N;
     const int64_t threads = (a.N % 4) == 0 ? total / 4 : total;
-    dgemm_reduce_kernel<HW && B != kFp16Bits><<<unsigned((threads + 255) / 256), 256, 0, s>>>(
-        a.part, a.S, a.M, a.N, m.scales, a.bias, a.y, a.y32);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned((threads + 255) / 256));
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, dgemm_reduce_kernel<HW && B != kFp16Bits>, a.part, a.S, a.M, a.N,
+                              m.scales, a.bias, a.y, a.y32);
 }
 }  // namespace
 
