@@ -359,8 +359,9 @@ class RuntimeMatrix:
     # -- execution -----------------------------------------------------------
     def _launch(self, x: torch.Tensor, M: int, bias: torch.Tensor | None, y: torch.Tensor,
                 y32: torch.Tensor | None) -> None:
-        # libebx selects the matrix's device itself; the stream is that device's current one
-        ws_bytes = int(_LIB.ebx_linear_workspace_bytes(self._h, M))
+        # libebx selects the matrix's device itself; the stream is that device's current one.
+        # Decode batches (M <= 16) never need a workspace: skip the query on that hot path.
+        ws_bytes = 0 if M <= 16 else int(_LIB.ebx_linear_workspace_bytes(self._h, M))
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=self._cuda) if ws_bytes else None
         _ebx.check(_LIB.ebx_linear(
             self._h, x.data_ptr(), M, None if bias is None else bias.data_ptr(), y.data_ptr(),
