@@ -161,9 +161,15 @@ def test_config1_backends_agree(cuda_ok):
 
     calib = torch.from_numpy(O.normal((64, 128, 384), seed=1)).cuda().half()
     x = torch.from_numpy(O.normal((2, 128, 384), seed=2)).cuda().half()
+    # the model path's selection restated by the oracle, on the FP16 weight and the first
+    # 32 calibration rows compress captures (core.py:734)
+    obits, _, oq, os_ = O.select_bits_torch(make()[0].weight.detach(),
+                                            calib[0, :32].float().cpu().numpy(), 0.01)
     ref_model = ElasticBit.compress(make(), calib, 0.01, backend="pytorch")
     nat_model = ElasticBit.compress(make(), calib, 0.01, backend="native")
-    assert ref_model[0].matrix.storageBits == nat_model[0].matrix.storageBits
+    assert ref_model[0].matrix.storageBits == nat_model[0].matrix.storageBits == obits
+    assert np.array_equal(nat_model[0].matrix.dequantize(),
+                          O.dequantize_codes(oq, os_).astype(np.float32))
     y_ref = ref_model(x).float().cpu().numpy()
     y_nat = nat_model(x).float().cpu().numpy()
     # north_star bar: relative L2 <= 1e-3, max-abs <= 2e-3 (or one fp16 ulp of
