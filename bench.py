@@ -15,7 +15,10 @@ measured through the public API (RuntimeMatrix.linear) with pinned host
 inputs/outputs copied every launch; ``roofline`` for the decode kernel against
 the measured HBM copy bandwidth; ``cpu_baseline`` = the reference's
 ``pytorch`` route restated on the host cores (F.linear over the dequantised
-weight, all threads) on a bounded sample.
+weight, all threads) on a bounded sample.  The same line also carries
+``prefill`` (TFLOP/s against the tensor roofline),
+``bolt_decoder`` (config 4, the BoltModel-shaped decoder, dense vs compressed)
+and ``tp_stack`` (config 5, the 8B-shaped stack under tensor parallelism).
 
 Multi-GPU (torchrun, --gpus N): every rank runs the same sweep on its own
 GPU (replicas; weak scaling); value = all ranks' bytes / max-over-ranks time.
@@ -543,8 +546,9 @@ def run_prefill(mats, device, lib, args) -> dict:
     big = [c for c in cases if c["M"] == 4096]
     agg = sum(2.0 * c["M"] * c["N"] * c["K"] for c in big) / (sum(c["ms"] for c in big) * 1e-3) / 1e12
     return {"workload": "config3: M in {256,1024,4096} x (K,N) in {(4096,4096),(4096,14336),"
-                        "(14336,4096)}, threshold 0.01; ebx_linear = exact fp16 materialise + "
-                        "tcgen05 GEMM; median of timed launches",
+                        "(14336,4096)}, threshold 0.01; ebx_linear routes M = 256 with K = 14336 "
+                        "to the decode-GEMM (codes decoded into tcgen05 tiles), the rest to exact "
+                        "fp16 materialise + tcgen05 GEMM; median of timed launches",
             "M4096_TFLOPs": round(agg, 1), "cases": cases,
             "roofline": {"bound": "tensor", "achieved": round(agg, 1), "peak": pk["bf16_tflops"],
                          "unit": "TFLOP/s", "frac": round(agg / pk["bf16_tflops"], 4),

@@ -385,8 +385,13 @@ __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, ui
 
 // A-fragment registers of one lane's 32 codes (register 4s + rr: codes 2(4s+rr),
 // +1; rr odd -> row r0 + 8) -> exact fp16 pairs.
+// Paired-decode constants of a b = 8..12 code (a placeholder width otherwise).
+template <int B>
+using DgConsts = PairConsts<(B >= 8 && B <= 12) ? B : 8>;
+
 template <int B, bool HW>
-__device__ __forceinline__ void dg_decode(const uint32_t (&w)[B], const uint64_t (&s2)[2], uint32_t (&af)[16]) {
+__device__ __forceinline__ void dg_decode(const uint32_t (&w)[B], const uint64_t (&s2)[2],
+                                          const DgConsts<B>& pk, uint32_t (&af)[16]) {
     if constexpr (B == kFp16Bits) {
 #pragma unroll
         for (int p = 0; p < 16; ++p) af[p] = w[p];
@@ -396,8 +401,6 @@ __device__ __forceinline__ void dg_decode(const uint32_t (&w)[B], const uint64_t
 #pragma unroll
         for (int p = 0; p < 16; ++p) af[p] = codes2_to_half(code_magic<B>(w, 2 * p), code_magic<B>(w, 2 * p + 1), nb2);
     } else if constexpr (B >= 8 && B <= 12) {
-        PairConsts<B> pk;
-        pk.init(0x4B000000u);
         uint32_t lo[4], hi[4];
         dequant_steps<B, 0>(w, pk, s2, lo, hi);
 #pragma unroll
@@ -524,6 +527,15 @@ __global__ void __launch_bounds__(kDgThreads, 2)
                 s2[h] = pack2f(sv, sv);
             }
         }
+        DgConsts<B> pk;  // built once: they depend on the width only
+        pk.init(0x4B000000u);
+        // byte offsets in the A tile of this lane's four 16-byte chunks: rows 16r + r0 (+8),
+        // k = 16c..16c+15 = chunks 2c, 2c+1, 128-byte swizzle
+        const int nlo = 16 * r + r0, nhi = nlo + 8;
+        const uint32_t o_lo0 = uint32_t(nlo * 128 + (((2 * c) ^ (nlo & 7)) << 4));
+        const uint32_t o_lo1 = uint32_t(nlo * 128 + (((2 * c + 1) ^ (nlo & 7)) << 4));
+        const uint32_t o_hi0 = uint32_t(nhi * 128 + (((2 * c) ^ (nhi & 7)) << 4));
+        const uint32_t o_hi1 = uint32_t(nhi * 128 + (((2 * c + 1) ^ (nhi & 7)) << 4));
         for (int i = 0; i < nkb; ++i) {
             const int st = i % D;
             if (!dg_wait(smem_u32(&full[st]), uint32_t(i / D) & 1u)) break;
@@ -545,17 +557,12 @@ __global__ void __launch_bounds__(kDgThreads, 2)
                     w[B - 1] = *reinterpret_cast<const uint32_t*>(cb + (B / 4) * 512 + ((B & 2) ? 256 : 0) +
                                                                   lane * 4);
                 uint32_t af[16];
-                dg_decode<B, HW>(w, s2, af);
-                // rows 16r + r0 (+8) of the A tile, k = 16c..16c+15: chunks 2c, 2c+1
+                dg_decode<B, HW>(w, s2, pk, af);
                 const uint32_t abase = smem_u32(stage);
-                const int nlo = 16 * r + r0, nhi = nlo + 8;
-                auto chunk = [&](int n, int j) {
-                    return abase + uint32_t(n * 128 + ((j ^ (n & 7)) << 4));
-                };
-                sts128(chunk(nlo, 2 * c), af[0], af[2], af[4], af[6]);
-                sts128(chunk(nlo, 2 * c + 1), af[8], af[10], af[12], af[14]);
-                sts128(chunk(nhi, 2 * c), af[1], af[3], af[5], af[7]);
-                sts128(chunk(nhi, 2 * c + 1), af[9], af[11], af[13], af[15]);
+                sts128(abase + o_lo0, af[0], af[2], af[4], af[6]);
+                sts128(abase + o_lo1, af[8], af[10], af[12], af[14]);
+                sts128(abase + o_hi0, af[1], af[3], af[5], af[7]);
+                sts128(abase + o_hi1, af[9], af[11], af[13], af[15]);
             }
             fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
             __syncwarp();
