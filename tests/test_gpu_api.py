@@ -2,6 +2,10 @@
 (tests/test_elasticbit_native.py in MLBricks) plus route parity."""
 from __future__ import annotations
 
+import io
+import json
+import zipfile
+
 import numpy as np
 import pytest
 import torch
@@ -95,6 +99,50 @@ def test_model_compress_switch_and_artifact(cuda_ok, tmp_path):
     ElasticBit.load(shell, artifact, decodePolicy="fullPrecision")
     restored = shell(x).detach()
     torch.testing.assert_close(restored, full, atol=0, rtol=0)
+
+
+# the reference writer's manifest and layer-entry keys, in its order
+# (mlbricks/elasticbit/core.py:928-947)
+REF_MANIFEST_KEYS = ["format", "version", "threshold", "decodePolicy", "compressedNames",
+                     "skippedNames", "optimizationProfiles", "layers"]
+REF_LAYER_KEYS = ["name", "matrix", "inFeatures", "outFeatures", "hasBias"]
+
+
+def test_model_artifact_layout_follows_reference_writer(cuda_ok, tmp_path):
+    torch.manual_seed(11)
+    model = torch.nn.Sequential(torch.nn.Linear(64, 96), torch.nn.GELU(),
+                                torch.nn.Linear(96, 40, bias=False)).cuda().half().eval()
+    ElasticBit.compress(model, [torch.randn(4, 64, device="cuda", dtype=torch.float16)], 0.03)
+    path = ElasticBit.save(model, tmp_path / "m.elasticbit")
+    with zipfile.ZipFile(path) as zf:
+        names = sorted(zf.namelist())
+        assert names == ["manifest.json", "matrices/matrix_00000.mlb", "matrices/matrix_00001.mlb",
+                         "state.pt"]
+        manifest = json.loads(zf.read("manifest.json"))
+        blobs = {n: zf.read(n) for n in names if n.endswith(".mlb")}
+        state = torch.load(io.BytesIO(zf.read("state.pt")), weights_only=True)
+    assert list(manifest) == REF_MANIFEST_KEYS
+    assert (manifest["format"], manifest["version"]) == ("ElasticBitModel", 1)
+    assert manifest["threshold"] == 0.03 and manifest["decodePolicy"] == "hardwareNative"
+    assert manifest["compressedNames"] == ["0", "2"] and manifest["skippedNames"] == []
+    for i, entry in enumerate(manifest["layers"]):
+        assert list(entry) == REF_LAYER_KEYS
+        layer = model[int(entry["name"])]
+        m = layer.matrix
+        assert entry["matrix"] == f"matrix_{i:05d}.mlb"
+        assert (entry["inFeatures"], entry["outFeatures"], entry["hasBias"]) == \
+            (layer.inFeatures, layer.outFeatures, layer.bias is not None)
+        parsed = O.mlb4_parse(blobs["matrices/" + entry["matrix"]])
+        assert (parsed["rows"], parsed["cols"], parsed["bits"]) == (m.rows, m.cols, m.storageBits)
+        assert parsed["threshold"] == 0.03 and parsed["selectedError"] == m.error
+        if m.storageBits == 16:
+            w = parsed["payload"].view(np.float16).reshape(m.rows, m.cols).astype(np.float32)
+        else:
+            codes = O.unpack_codes(parsed["payload"], m.rows, m.cols, m.storageBits)
+            w = O.dequantize_codes(codes, parsed["scales"]).astype(np.float32)
+        assert np.array_equal(w, m.dequantize())
+    assert set(state) == set(model.state_dict()) == {"0.bias"}
+    torch.testing.assert_close(state["0.bias"], model[0].bias, atol=0, rtol=0)
 
 
 def test_model_analyzer_result_reuse_and_policy(cuda_ok, tmp_path):
