@@ -150,9 +150,14 @@ EBX_API ebx_status ebx_analyze(const float* weights, int32_t rows, int32_t cols,
  * ebx_analyze; the scratch is a fixed 8 MiB array inside the library that
  * every GPU loading it keeps until the process exits, so the call needs
  * 256-byte-rounded 4*rows*samples + 336*rows bytes <= 8 MiB (e.g. 8192 rows x
- * 32 samples) and returns EBX_ERR_INVALID with a message beyond that.  The
- * first call on a device looks up the array's device address (with that
- * device current); make that first call before any stream capture.  All
+ * 32 samples) and returns EBX_ERR_INVALID with a message beyond that (an
+ * argument-size error, unlike ebx_analyze's EBX_ERR_WORKSPACE, which reports a
+ * caller workspace that is too small).  The first call on a device looks up
+ * the array's device address (with that device current) and keeps it for the
+ * life of the process; make that first call before any stream capture, and
+ * make no call after a cudaDeviceReset of that device (the reset frees the
+ * array and the kept address goes stale, like every other device object of
+ * this library).  All
  * calls on a device share the array: calls whose kernels overlap on the GPU
  * (different streams without ordering) race and give wrong results. */
 EBX_API ebx_status ebx_analyze_noalloc(const float* weights, int32_t rows, int32_t cols,
@@ -223,9 +228,12 @@ EBX_API ebx_status ebx_linear_swiglu(const ebx_matrix* m, const void* x, int64_t
  *      ranks, sums the partials in rank order 0..world-1, adds bias in fp32
  *      and rounds once to fp16.  Every rank gets bit-identical outputs.
  *
- * All ranks must issue the same sequence of ebx_linear_allreduce calls with
- * the same M and shard shape; the epoch lives in device memory, so the calls
- * may be captured in a CUDA graph.  Ranks must be on distinct GPUs (connect
+ * All ranks must issue the same sequence of ebx_linear_allreduce calls, each
+ * call with the same M and shard shape on every rank; M and the shard's rows
+ * may change from one call to the next (up to max_m and max_n), because the
+ * two partial slots are laid out with the exchange's fixed max_m * max_n
+ * stride.  The epoch lives in device memory, so the calls may be captured in a
+ * CUDA graph.  Ranks must be on distinct GPUs (connect
  * refuses otherwise).  A wait that gives up sets the device status word
  * (ebx_device_status) and leaves y unwritten; the exchange is then out of
  * step and must be destroyed. */

@@ -220,7 +220,9 @@ static __device__ __align__(256) unsigned char g_analyze_scratch[kNoAllocScratch
 
 // In host code `g_analyze_scratch` names a host-side stand-in, not device
 // memory; the device address comes from cudaGetSymbolAddress, taken once per
-// device with that device current.
+// device with that device current and kept for the process (a cudaDeviceReset
+// would free the array and leave the kept address stale; the header forbids
+// calls after one).
 std::mutex g_noalloc_mutex;
 void* g_noalloc_ptr[64] = {};
 

@@ -474,6 +474,7 @@ ebx_status ebx_exchange_create(int32_t world, int32_t rank, int32_t device, int6
     ex->max_n = max_n;
     ex->xa.world = world;
     ex->xa.rank = rank;
+    ex->xa.slot_words = max_m * max_n;
     ex->bytes = ebx::kXchgDataOff + 2ull * uint64_t(world) * uint64_t(max_m) * uint64_t(max_n) * 8ull;
     cudaError_t e = cudaMalloc(&ex->own, ex->bytes);
     if (e == cudaSuccess) e = cudaMemset(ex->own, 0, ex->bytes);

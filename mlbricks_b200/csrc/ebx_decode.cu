@@ -655,35 +655,6 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
 
 constexpr int kStages = 4;
 
-// Runtime knobs of the decode launcher, read once per process:
-//   EBX_PDL=0             launch without programmatic dependent launch
-//   EBX_PDL_TRIGGER=early signal dependents at the start of each CTA (default:
-//                         once its main loop is done)
-//   EBX_M4_MINB=2|3       M <= 4: CTAs per SM (default: 2 when the grid is then one
-//                         wave and K <= 8192, else 3)
-//   EBX_M8_MINB=2|3       4 < M <= 8: CTAs per SM (default 2: two supertiles per
-//                         warp and round; 3: one)
-//   EBX_M16_MINB=2|3      8 < M <= 16: CTAs per SM (default: as for M <= 4)
-struct DecodeKnobs {
-    bool pdl = true;
-    bool early = false;
-    int m4_minb = 0;
-    int m8_minb = 2;
-    int m16_minb = 0;
-};
-const DecodeKnobs& decode_knobs() {
-    static const DecodeKnobs k = [] {
-        DecodeKnobs v;
-        if (const char* e = std::getenv("EBX_PDL")) v.pdl = std::atoi(e) != 0;
-        if (const char* e = std::getenv("EBX_PDL_TRIGGER")) v.early = std::strcmp(e, "early") == 0;
-        if (const char* e = std::getenv("EBX_M4_MINB")) v.m4_minb = std::atoi(e) == 2 ? 2 : 3;
-        if (const char* e = std::getenv("EBX_M8_MINB")) v.m8_minb = std::atoi(e) == 3 ? 3 : 2;
-        if (const char* e = std::getenv("EBX_M16_MINB")) v.m16_minb = std::atoi(e) == 2 ? 2 : 3;
-        return v;
-    }();
-    return k;
-}
-
 // Multiprocessors of the current device (cached per device).
 int sm_count() {
     static std::atomic<int> cache[64];
@@ -718,8 +689,8 @@ cudaError_t launch_maybe_xchg(Kern kern, DecodeArgs& a, unsigned grid, unsigned 
         cfg.attrs = attr;
         // measured: overlapping helps when a CTA's run is short (K <= 8192) and costs
         // 5-8 % when it is long (K = 14336: next grid's CTAs land unevenly)
-        cfg.numAttrs = pdl && decode_knobs().pdl && a.kt <= 128 ? 1 : 0;
-        a.pdl_early = decode_knobs().early ? 1 : 0;
+        cfg.numAttrs = pdl && a.kt <= 128 ? 1 : 0;
+        a.pdl_early = 0;
         return cudaLaunchKernelEx(&cfg, kern, a);
     }
     int dev = 0, sms = 0, per_sm = 0;
@@ -803,14 +774,13 @@ cudaError_t dispatch_nt(DecodeArgs& a, int groups, bool pipe, bool direct, cudaS
         // whose 448-CTA grid for N = 14336 runs in 3.03 waves).
         // (8..12-bit full semantics decode in pairs and ignore `direct`)
         constexpr bool kCanDirect = !HW && B != kFp16Bits && !(B >= 8 && B <= 12);
-        const DecodeKnobs& kn = decode_knobs();
         // Two CTAs per SM (a deeper ring, up to 113 registers) pay off when the grid
         // is then still one wave and each CTA's run is short (measured on the
         // BASELINE shapes: 4096x4096 12 % faster; 14336-row and 14336-column
         // matrices slower), else three CTAs per SM.
         const bool two_per_sm = groups <= 2 * sm_count() && a.kt <= 128;
         if (B <= 12 && a.M <= 4) {
-            if (kn.m4_minb == 2 || (kn.m4_minb == 0 && two_per_sm))
+            if (two_per_sm)
                 return launch_pipe<B, HW, 1, false, 1, 2, 2>(a, groups, s);
             if constexpr (kCanDirect)
                 if (direct) return launch_pipe<B, HW, 1, true, 1, 2>(a, groups, s);
@@ -819,8 +789,7 @@ cudaError_t dispatch_nt(DecodeArgs& a, int groups, bool pipe, bool direct, cudaS
         if (a.M <= 8) {
             // two CTAs per SM with two supertiles per warp and round (measured 13-22 %
             // faster than three CTAs with one supertile on the BASELINE decode shapes)
-            if constexpr (B <= 12)
-                if (kn.m8_minb == 2) return launch_pipe<B, HW, 1, false, 1, 2, 2>(a, groups, s);
+            if constexpr (B <= 12) return launch_pipe<B, HW, 1, false, 1, 2, 2>(a, groups, s);
             if constexpr (kCanDirect)
                 if (direct) return launch_pipe<B, HW, 1, true, 1, 1>(a, groups, s);
             return launch_pipe<B, HW, 1, false, 1, 1>(a, groups, s);
@@ -829,7 +798,7 @@ cudaError_t dispatch_nt(DecodeArgs& a, int groups, bool pipe, bool direct, cudaS
             return launch_pipe<B, HW, 2, false, 2, 1>(a, groups, s);
         // 16 activation rows: two CTAs per SM (a three-stage ring) under the same
         // rule, else three CTAs per SM (two stages)
-        if (kn.m16_minb == 2 || (kn.m16_minb == 0 && two_per_sm))
+        if (two_per_sm)
             return launch_pipe<B, HW, 2, false, 1, 1, 2>(a, groups, s);
         if constexpr (kCanDirect)
             if (direct) return launch_pipe<B, HW, 2, true, 1, 1>(a, groups, s);

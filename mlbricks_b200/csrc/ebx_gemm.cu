@@ -680,11 +680,6 @@ DgPlan dg_plan(const Matrix& m, int64_t M, int sms) {
     // Two CTAs per SM when each can still hold a ring of two or three stages
     // (measured: more stages at one CTA per SM do not help), else one CTA with up to six.
     constexpr int kOverhead = 1024 + 256;
-    static const int cap_env = [] {  // EBX_DG_STAGES=n caps the ring depth (measurement knob)
-        const char* e = std::getenv("EBX_DG_STAGES");
-        const int v = e ? std::atoi(e) : 0;
-        return v >= 2 && v <= 12 ? v : 0;
-    }();
     int per_sm = 1;
     int D = (227 * 1024 - kOverhead) / p.stage_bytes;
     D = D > 6 ? 6 : D;
@@ -693,7 +688,6 @@ DgPlan dg_plan(const Matrix& m, int64_t M, int sms) {
         per_sm = 2;
         D = D2 > 3 ? 3 : D2;
     }
-    if (cap_env && D > cap_env) D = cap_env;
     p.stages = D;
     p.smem = D * p.stage_bytes + kOverhead;
     // K split: minimise (waves x k-blocks per split) x ~0.5 us + the fp32 partials'

@@ -56,6 +56,7 @@ struct XchgArgs {
     int world = 0;             // 0: no exchange (plain y / y32 output)
     int rank = 0;
     int fused = 0;             // set by the launcher: the decode kernel also reduces (grid co-resident)
+    int64_t slot_words = 0;    // words per (slot, source rank): max_m * max_n of the exchange
 };
 
 // ebx_decode.cu -------------------------------------------------------------

@@ -10,6 +10,13 @@
 // E + 1 needs every rank's partials of E + 1, which each rank produces only
 // after its own exchange E is complete.
 //
+// Slot layout: slot (e & 1) of source rank r starts at word
+// ((e & 1) * world + r) * slot_words, with slot_words = max_m * max_n of the
+// exchange, and word tok * N + row inside it holds (tok, row) of the current
+// call.  The slot stride is fixed by the exchange, not by the call, so calls
+// of different M or N on one exchange never overlap: a rank one exchange ahead
+// writes only slot (E + 1) & 1 while a slower peer still reads slot E & 1.
+//
 // The epoch lives in device memory (so CUDA graph replays advance it): every
 // CTA reads it at its start, and the last CTA of the kernel that completes an
 // exchange (the fused decode kernel, or the finish kernel) stores epoch + 1.
@@ -40,11 +47,13 @@ __device__ __forceinline__ uint32_t xchg_epoch(const XchgArgs& xa) {
     return *reinterpret_cast<volatile const uint32_t*>(xa.peer[xa.rank] + kXchgEpochOff);
 }
 
-// Words of source rank `src` for epoch `e` inside a region: [M][N].
-__device__ __forceinline__ uint64_t* xchg_words(uint8_t* region, uint32_t e, int world, int src,
-                                                int M, int N) {
+// Words of source rank `src` for epoch `e` inside a region (slot stride
+// xa.slot_words = max_m * max_n of the exchange; the call's [M][N] words fill
+// the start of the slot).
+__device__ __forceinline__ uint64_t* xchg_words(const XchgArgs& xa, uint8_t* region, uint32_t e,
+                                                int src) {
     return reinterpret_cast<uint64_t*>(region + kXchgDataOff) +
-           (size_t(e & 1u) * size_t(world) + size_t(src)) * size_t(M) * size_t(N);
+           (size_t(e & 1u) * size_t(xa.world) + size_t(src)) * size_t(xa.slot_words);
 }
 
 // Store this rank's partial of (tok, row) for epoch e into every rank's region.
@@ -54,7 +63,7 @@ __device__ __forceinline__ void xchg_push(const XchgArgs& xa, uint32_t e, int M,
     const size_t off = size_t(tok) * size_t(N) + size_t(row);
 #pragma unroll 1
     for (int q = 0; q < xa.world; ++q)
-        st_relaxed_sys_u64(xchg_words(xa.peer[q], e, xa.world, xa.rank, M, N) + off, w);
+        st_relaxed_sys_u64(xchg_words(xa, xa.peer[q], e, xa.rank) + off, w);
 }
 
 // Sum of all ranks' partials of (tok, row) for epoch e, in rank order 0..world-1
@@ -68,7 +77,7 @@ __device__ __forceinline__ bool xchg_gather(const XchgArgs& xa, uint32_t e, int 
     uint64_t t0 = 0;
 #pragma unroll 1
     for (int r = 0; r < xa.world; ++r) {
-        const uint64_t* p = xchg_words(own, e, xa.world, r, M, N) + off;
+        const uint64_t* p = xchg_words(xa, own, e, r) + off;
         uint64_t w = ld_relaxed_sys_u64(p);
         while (uint32_t(w >> 32) != e) {
             const uint64_t now = global_ns();

@@ -309,6 +309,15 @@ class RuntimeMatrix:
     error = property(lambda self: float(self._native.error))
 
 
+def _row_regime(rows: int) -> str:
+    """Row-count regime an `auto` decision is frozen for: the native kernels
+    differ by regime (decode GEMV, decode-GEMM, prefill GEMM), so a race won on
+    a 4096-token prefill says nothing about a one-token decode step."""
+    if rows <= 16:
+        return "decode"
+    return "small-batch" if rows <= 256 else "prefill"
+
+
 class _ElasticLinear(nn.Module):
     """Internal replacement for nn.Linear.  Not part of the public import surface.
 
@@ -367,11 +376,12 @@ class _ElasticLinear(nn.Module):
             return self._forward_native(x)
         from ..planner import EXECUTION_PLANNER
 
+        rows = int(x.numel() // self.inFeatures)
         route = EXECUTION_PLANNER.qualify_operator_once(
             self, "elastic_linear", x,
             {"native": lambda: self._forward_native(x), "pytorch": lambda: self._forward_pytorch(x)},
             requested_backend="auto", native_available=True, training=False,
-            extra=(self.inFeatures, self.outFeatures, int(x.numel() // self.inFeatures)),
+            extra=(self.inFeatures, self.outFeatures, rows), freeze_on=(_row_regime(rows),),
         )
         return self._forward_native(x) if route == "native" else self._forward_pytorch(x)
 

@@ -161,7 +161,14 @@ class MLBricksExecutionPlanner:
                               extra: tuple[object, ...] = (), default_auto: str | None = None,
                               warmup: int = 2, trials: int = 5, switch_margin: float = 0.05,
                               verify_parity: bool = True, parity_rtol: float | None = None,
-                              parity_atol: float | None = None) -> str:
+                              parity_atol: float | None = None,
+                              freeze_on: tuple[object, ...] = ()) -> str:
+        """One parity-checked timing race per (op, training, *freeze_on), then frozen.
+
+        ``freeze_on`` names the regime a decision holds for (for example the
+        row-count regime of a linear): each distinct value races and freezes on
+        its own, so a decision taken on one regime never routes another.
+        """
         policy = normalize_backend(requested_backend, warn_legacy=True)
         is_training = bool(torch.is_grad_enabled()) if training is None else bool(training)
         common = dict(native_available=native_available,
@@ -180,7 +187,7 @@ class MLBricksExecutionPlanner:
                 setattr(owner, "_mlbricks_frozen_auto_routes", cache)
             except Exception:
                 pass
-        fkey = (str(op), bool(is_training))
+        fkey = (str(op), bool(is_training), *freeze_on)
         if cache.get(fkey) in {"native", "pytorch"}:
             return cache[fkey]
         usable = {n: f for n, f in candidates.items() if n in {"native", "pytorch"} and callable(f)}

@@ -23,8 +23,13 @@ HERE = Path(__file__).resolve().parent
 BUILD_DIR = HERE / "_build"
 REF_DIR = HERE / "_ref"
 ORACLE_SO = BUILD_DIR / "libebx_oracle.so"
-REFERENCE_ROOT = Path(os.environ.get("EBX_REFERENCE_ROOT", "/root/reference"))
-REFERENCE_CU = REFERENCE_ROOT / "mlbricks" / "elasticbit" / "csrc" / "elasticbit_runtime.cu"
+REFERENCE_CU_REL = Path("mlbricks") / "elasticbit" / "csrc" / "elasticbit_runtime.cu"
+
+
+def reference_root(explicit: str | os.PathLike | None = None) -> Path | None:
+    """The MLBricks source tree: `explicit`, else $EBX_REFERENCE_ROOT, else None."""
+    root = explicit if explicit is not None else os.environ.get("EBX_REFERENCE_ROOT")
+    return Path(root) if root else None
 
 
 def build_oracle(force: bool = False) -> Path:
@@ -40,16 +45,21 @@ def build_oracle(force: bool = False) -> Path:
     return ORACLE_SO
 
 
-def build_reference(force: bool = False, verbose: bool = False) -> Path | None:
+def build_reference(root: str | os.PathLike | None = None, force: bool = False,
+                    verbose: bool = False) -> Path | None:
     """Compile the reference ElasticBit runtime into oracle/_ref/_C.so.
 
-    Returns the path, or None when the reference tree is absent (GPU box).
-    Skips the ~3 minute nvcc build when the output matches the source hash.
+    `root` is the MLBricks source tree (default: $EBX_REFERENCE_ROOT).  Returns
+    the path, or the previously built library (or None) when no tree is given
+    or it is absent (as on a GPU box).  Skips the ~3 minute nvcc build when the
+    output matches the source hash.
     """
     out = REF_DIR / "_C.so"
-    if not REFERENCE_CU.exists():
+    tree = reference_root(root)
+    reference_cu = tree / REFERENCE_CU_REL if tree else None
+    if reference_cu is None or not reference_cu.exists():
         return out if out.exists() else None
-    digest = hashlib.sha256(REFERENCE_CU.read_bytes()).hexdigest()
+    digest = hashlib.sha256(reference_cu.read_bytes()).hexdigest()
     stamp = REF_DIR / "source.sha256"
     if not force and out.exists() and stamp.exists() and stamp.read_text().strip() == digest:
         return out
@@ -58,7 +68,7 @@ def build_reference(force: bool = False, verbose: bool = False) -> Path | None:
 
     load(
         name="_C",
-        sources=[str(REFERENCE_CU)],
+        sources=[str(reference_cu)],
         build_directory=str(REF_DIR),
         extra_cflags=["-O3"],
         extra_cuda_cflags=["-O3", "--use_fast_math",
@@ -71,6 +81,9 @@ def build_reference(force: bool = False, verbose: bool = False) -> Path | None:
 
 
 if __name__ == "__main__":
+    # python oracle/build.py [--force] [--reference MLBRICKS_TREE]
     print(build_oracle(force="--force" in sys.argv))
     if "--reference" in sys.argv:
-        print(build_reference(force="--force" in sys.argv, verbose=True))
+        i = sys.argv.index("--reference")
+        tree = sys.argv[i + 1] if i + 1 < len(sys.argv) else None
+        print(build_reference(tree, force="--force" in sys.argv, verbose=True))

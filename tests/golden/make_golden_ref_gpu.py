@@ -12,8 +12,8 @@ a GPU machine and records, for seeded small cases:
   ``fullPrecision`` (base64 of the fp16 bytes);
 * for ``RuntimeMatrix.compress`` (matrix path): the selected width and error.
 
-Usage (GPU machine, repo root):
-    python tests/golden/make_golden_ref_gpu.py gpurun_out/ref_gpu_golden.json
+Usage (GPU machine, repo root; OUT is any writable path):
+    python tests/golden/make_golden_ref_gpu.py OUT.json
 then copy the JSON to tests/golden/ref_gpu_golden.json.
 """
 from __future__ import annotations
@@ -113,4 +113,6 @@ def main(out_path: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "gpurun_out/ref_gpu_golden.json")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden_ref_gpu.py OUT.json")
+    main(sys.argv[1])

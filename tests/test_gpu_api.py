@@ -226,3 +226,38 @@ def test_config1_backends_agree(cuda_ok):
     assert rel <= 1e-3
     ulp = np.spacing(np.abs(y_ref.astype(np.float16))).astype(np.float32)
     assert np.all(np.abs(y_nat - y_ref) <= np.maximum(2e-3, ulp))
+
+
+def test_auto_route_decides_per_row_regime(cuda_ok):
+    """`auto` races once per row regime: a prefill-sized call whose native
+    candidate is made slow freezes `pytorch` for prefill only, and the first
+    decode call still races and goes native (the per-call materialise of the
+    pytorch route is far slower for one token)."""
+    import time
+
+    from mlbricks_b200.elasticbit.core import _ElasticLinear
+
+    rows, cols = 1024, 2048
+    w = O.baseline_weights(rows, cols, seed=41)
+    model = torch.nn.Sequential(torch.nn.Linear(cols, rows, bias=False)).cuda().half().eval()
+    with torch.no_grad():
+        model[0].weight.copy_(torch.from_numpy(w))
+    calib = torch.from_numpy(O.normal((32, cols), seed=42)).cuda().half()
+    ElasticBit.compress(model, calib, 0.01, backend="auto")
+    layer = model[0]
+    assert isinstance(layer, _ElasticLinear)
+    native = layer._forward_native
+
+    def slow_for_prefill(x):
+        if x.numel() // cols > 256:
+            torch.cuda.synchronize()
+            time.sleep(0.05)
+        return native(x)
+
+    layer._forward_native = slow_for_prefill
+    with torch.no_grad():
+        model(torch.from_numpy(O.normal((1024, cols), seed=43)).cuda().half())
+        model(torch.from_numpy(O.normal((1, cols), seed=44)).cuda().half())
+    routes = layer._mlbricks_frozen_auto_routes
+    assert routes[("elastic_linear", False, "prefill")] == "pytorch"
+    assert routes[("elastic_linear", False, "decode")] == "native"

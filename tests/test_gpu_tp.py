@@ -140,6 +140,75 @@ def test_tensor_parallel_matches_single_gpu(cuda_ok):
                 assert np.array_equal(y0, results[0][(M, "exchange", 0)])
 
 
+SEQ_MS = (16, 1, 8, 1, 5, 16, 2, 16)  # back-to-back exchange calls of changing M
+
+
+def _seq_inputs():
+    from oracle import oracle as O
+
+    _, K, _ = SHAPE
+    return [O.normal((M, K), seed=200 + i).astype(np.float16) for i, M in enumerate(SEQ_MS)]
+
+
+def _sequence_worker(rank, world, port, q_out):
+    """Exchange calls with a different M each, issued without any host
+    synchronisation in between; every rank but 0 sleeps on the host before
+    each launch, so rank 0 runs ahead and pushes the partials of call E + 1
+    while its peers still read those of call E."""
+    import ctypes
+    import time
+
+    dist = _init(rank, world, port)
+    from mlbricks_b200 import _ebx
+    from mlbricks_b200.elasticbit import tensor_parallel as tp
+
+    try:
+        q, s, bits, bias, _ = _case()
+        bias_t = torch.from_numpy(bias).cuda()
+        ex = tp.Exchange.from_group(16, 4096)
+        lin = tp.build_sharded(q, s, bits, "row", world, rank, bias=bias_t, exchange=ex)
+        xs = [torch.from_numpy(x).cuda() for x in _seq_inputs()]
+        torch.cuda.synchronize()
+        dist.barrier()
+        outs = []
+        for x in xs:
+            if rank != 0:
+                time.sleep(0.05)
+            outs.append(lin(x))
+        torch.cuda.synchronize()
+        res = {"y": [o.float().cpu().numpy() for o in outs]}
+        lib = _ebx.load()
+        v = ctypes.c_int32()
+        _ebx.check(lib.ebx_device_status(rank, ctypes.byref(v), 0))
+        res["status"] = int(v.value)
+        dist.barrier()
+        ex.close()
+        q_out.put((rank, res))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_exchange_back_to_back_changing_m(cuda_ok):
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("needs at least two GPUs")
+    results = _spawn(_sequence_worker, world)
+    from mlbricks_b200 import RuntimeMatrix
+
+    q, s, bits, bias, _ = _case()
+    full = RuntimeMatrix._compressSelectedCodes(q, s, bits, 0.0, 0.0, decodePolicy="fullPrecision")
+    b = torch.from_numpy(bias).cuda()
+    for i, x in enumerate(_seq_inputs()):
+        ref = full.linear(torch.from_numpy(x).cuda(), b).float().cpu().numpy()
+        tol = np.maximum(2e-3, np.spacing(np.abs(ref.astype(np.float16))).astype(np.float32))
+        for rank in range(world):
+            assert results[rank]["status"] == 0, rank
+            y = results[rank]["y"][i]
+            assert np.all(np.abs(y - ref) <= tol), (i, SEQ_MS[i], rank)
+            assert np.array_equal(y, results[0]["y"][i])
+
+
 def _absent_rank_worker(rank, world, port, q_out):
     dist = _init(rank, world, port)
     import ctypes
