@@ -287,8 +287,12 @@ ebx_status ebx_matrix_set_execution_width(ebx_matrix* h, int32_t width) {
         set_error("null matrix");
         return EBX_ERR_INVALID;
     }
-    if (width != 4 && width != 8 && width != 16) {
-        set_error("ElasticBit execution width must be 4, 8, or 16");
+    if (width != 4 && width != 8 && width != 12 && width != 16) {
+        set_error("ElasticBit execution width must be 4, 8, 12, or 16");
+        return EBX_ERR_INVALID;
+    }
+    if (width == 12 && h->m.bits > 12) {
+        set_error("W12A16 cannot represent this ElasticBit storage width");
         return EBX_ERR_INVALID;
     }
     if (width == 4 && h->m.bits > 4) {

@@ -504,3 +504,194 @@ __device__ __forceinline__ void dequant_steps(const uint32_t (&w)[B], const Pair
 }
 
 }  // namespace ebx
+
+namespace ebx {
+
+// ---------------------------------------------------------------------------
+// Plane layout (b = 9..12)
+// ---------------------------------------------------------------------------
+// Same supertiles, same 32 codes per lane, same b words per lane in the same
+// vector segments as the bitstream layout above (so every size and offset is
+// unchanged), but the bits of code j are split into planes so that the decode
+// can build fp16 operands with byte permutes instead of per-code shifts:
+//   low plane, words 0..7:  byte (j & 3) of word (j >> 2) = low 8 bits of code j;
+//   high plane, words 8..b-1 = the remaining b - 8 bits of code j (bit k = bit 8+k):
+//     b = 9:  bit 8*(j & 3) + (j >> 2) of word 8;
+//     b = 10: bits 8*(j & 3) + 2*((j >> 2) & 3) + k of word 8 + (j >> 4);
+//     b = 11: pair p = j >> 1 (codes 2p, 2p+1 share an A-fragment register),
+//             side = j & 1: p < 15 -> bit 16*side + 3*(p % 5) + k of word 8 + p / 5;
+//             p = 15 -> bit 15 + 16*side of word 8 + k;
+//     b = 12: bit 16*side + 4*(p % 4) + k of word 8 + p / 4.
+// For b = 9, 10 the high bits of codes 4i..4i+3 sit one per byte after one
+// shift, so (shifted & mask) | 0x64646464 gives each code its fp16 upper byte
+// (exponent of 1024 plus the top mantissa bits): one byte permute per pair then
+// yields fp16(1024 + code) exactly.  For b = 11, 12 (codes up to 2046 / 4094
+// do not fit one fp16 binade) the high part of a pair is one LOP3 away from
+// fp16x2(1024 + hi) and q = 256 * (hi - h0) + (lo - l0) is one fp16 FMA, exact
+// because every intermediate is an integer of magnitude below 2048.
+// b = 8's bitstream layout already is the low plane alone.
+__host__ __device__ constexpr bool plane_layout(int bits) { return bits >= 9 && bits <= 12; }
+
+// Word and bit of high bit k (0 .. bits-9) of code j in the plane layout.
+__host__ __device__ inline void plane_hi_bit(int bits, int j, int k, int* word, int* bit) {
+    const int p = j >> 1, side = j & 1;
+    if (bits == 9) {
+        *word = 8;
+        *bit = 8 * (j & 3) + (j >> 2);
+    } else if (bits == 10) {
+        *word = 8 + (j >> 4);
+        *bit = 8 * (j & 3) + 2 * ((j >> 2) & 3) + k;
+    } else if (bits == 11) {
+        if (p < 15) {
+            *word = 8 + p / 5;
+            *bit = 16 * side + 3 * (p % 5) + k;
+        } else {
+            *word = 8 + k;
+            *bit = 15 + 16 * side;
+        }
+    } else {
+        *word = 8 + p / 4;
+        *bit = 16 * side + 4 * (p % 4) + k;
+    }
+}
+
+// fp16 bit pattern of a small integer (|n| < 2048, exactly representable).
+__host__ __device__ constexpr uint32_t half_bits_int(int n) {
+    const uint32_t sign = n < 0 ? 0x8000u : 0u;
+    const uint32_t a = uint32_t(n < 0 ? -n : n);
+    if (a == 0) return sign;
+    int e = 0;
+    while ((a >> (e + 1)) != 0) ++e;
+    const uint32_t mant = ((a << (10 - e)) - 1024u) & 0x3FFu;
+    return sign | (uint32_t(e + 15) << 10) | mant;
+}
+__host__ __device__ constexpr uint32_t half2_bits_int(int n) {
+    return half_bits_int(n) | (half_bits_int(n) << 16);
+}
+
+template <uint32_t MASK>
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t c) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "n"(MASK), "r"(c));  // (a & MASK) | c
+    return d;
+}
+__device__ __forceinline__ uint32_t hsub2_u(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Constants of the plane decode, built once per thread from the run-time word
+// 0x64646464 (kept in registers instead of being re-materialised per use).
+struct PlaneConsts {
+    uint32_t k64;    // 0x64646464: fp16 upper byte of 1024 in every byte
+    uint32_t k6400;  // 0x64006400: fp16x2 (1024, 1024)
+    __device__ __forceinline__ void init(uint32_t k64_word) {
+        k64 = k64_word;
+        k6400 = k64_word & 0xFF00FF00u;
+    }
+};
+
+// Upper bytes (0x64 | high bits) of codes 4I .. 4I+3 (b = 9, 10); 0x64 bytes for b = 8.
+template <int B, int I>
+__device__ __forceinline__ uint32_t plane_hb(const uint32_t (&w)[B], const PlaneConsts& k) {
+    if constexpr (B == 8) {
+        return k.k64;
+    } else if constexpr (B == 9) {
+        return lop3_and_or<0x01010101u>(I == 0 ? w[8] : (w[8] >> I), k.k64);
+    } else {
+        static_assert(B == 10, "byte-plane high bits cover b = 9, 10");
+        constexpr int sh = 2 * (I & 3);
+        const uint32_t h = w[8 + (I >> 2)];
+        return lop3_and_or<0x03030303u>(sh == 0 ? h : (h >> sh), k.k64);
+    }
+}
+
+// fp16x2 (1024 + hi) of the high parts of pair P (b = 11, 12).
+template <int B, int P>
+__device__ __forceinline__ uint32_t plane_hi_pair(const uint32_t (&w)[B], const PlaneConsts& k) {
+    if constexpr (B == 12) {
+        constexpr int sh = 4 * (P % 4);
+        const uint32_t h = w[8 + P / 4];
+        return lop3_and_or<0x000F000Fu>(sh == 0 ? h : (h >> sh), k.k6400);
+    } else {
+        static_assert(B == 11, "pair high parts cover b = 11, 12");
+        if constexpr (P < 15) {
+            constexpr int sh = 3 * (P % 5);
+            const uint32_t h = w[8 + P / 5];
+            return lop3_and_or<0x00070007u>(sh == 0 ? h : (h >> sh), k.k6400);
+        } else {
+            uint32_t t = lop3_and_or<0x00010001u>(w[8] >> 15, k.k6400);
+            t = lop3_and_or<0x00020002u>(w[9] >> 14, t);
+            return lop3_and_or<0x00040004u>(w[10] >> 13, t);
+        }
+    }
+}
+
+// q = code - qmax of codes 2P, 2P+1 as exact fp16x2 (low half = code 2P), b = 8..12.
+template <int B, int P>
+__device__ __forceinline__ uint32_t plane_q16(const uint32_t (&w)[B], const PlaneConsts& k,
+                                              uint32_t hb) {
+    constexpr uint32_t kSel = (P & 1) ? 0x7362u : 0x5140u;
+    if constexpr (B <= 10) {
+        // (1024 + code) - (1024 + qmax)
+        const uint32_t v = __byte_perm(w[P >> 1], hb, kSel);
+        return hsub2_u(v, half2_bits_int(1024 + qmax_for(B)));
+    } else {
+        // qmax = 256 * h0 + l0 with h0 = 2^(B-9), l0 = -1
+        constexpr int h0 = 1 << (B - 9);
+        const uint32_t lo = hsub2_u(__byte_perm(w[P >> 1], k.k64, kSel), half2_bits_int(1023));
+        const uint32_t hi = hsub2_u(plane_hi_pair<B, P>(w, k), half2_bits_int(1024 + h0));
+        return hfma2_u(hi, half2_bits_int(256), lo);
+    }
+}
+
+// Pairs 2I, 2I+1 (codes 4I .. 4I+3) of a lane's slice, exact fp16x2 q.
+template <int B, int I>
+__device__ __forceinline__ void plane_quad(const uint32_t (&w)[B], const PlaneConsts& k,
+                                           uint32_t (&q16)[16]) {
+    uint32_t hb = 0;
+    if constexpr (B <= 10) hb = plane_hb<B, I>(w, k);
+    q16[2 * I] = plane_q16<B, 2 * I>(w, k, hb);
+    q16[2 * I + 1] = plane_q16<B, 2 * I + 1>(w, k, hb);
+}
+
+// All 16 pairs of a lane's slice: q16[p] = fp16x2 q of codes 2p, 2p+1
+// (A-fragment register p: k-step p / 4, register p % 4).
+template <int B>
+__device__ __forceinline__ void plane_q16_all(const uint32_t (&w)[B], const PlaneConsts& k,
+                                              uint32_t (&q16)[16]) {
+    plane_quad<B, 0>(w, k, q16);
+    plane_quad<B, 1>(w, k, q16);
+    plane_quad<B, 2>(w, k, q16);
+    plane_quad<B, 3>(w, k, q16);
+    plane_quad<B, 4>(w, k, q16);
+    plane_quad<B, 5>(w, k, q16);
+    plane_quad<B, 6>(w, k, q16);
+    plane_quad<B, 7>(w, k, q16);
+}
+
+// Exact W16 operand from an exact q pair: fp16_rn(fp32_rn(float(q) * s)) for
+// both halves (the reference's static_cast<float>(q) * scale, then
+// __float2half_rn); s2 = (s, s) of the pair's row.
+__device__ __forceinline__ uint32_t q16_to_w16(uint32_t q16, uint64_t s2) {
+    uint32_t h;
+    asm("{\n\t.reg .b16 l, u;\n\t.reg .f32 fl, fu;\n\t.reg .b64 a;\n\t"
+        "mov.b32 {l, u}, %1;\n\t"
+        "cvt.f32.f16 fl, l;\n\t"
+        "cvt.f32.f16 fu, u;\n\t"
+        "mov.b64 a, {fl, fu};\n\t"
+        "mul.rn.f32x2 a, a, %2;\n\t"
+        "mov.b64 {fl, fu}, a;\n\t"
+        "cvt.rn.f16x2.f32 %0, fu, fl;\n\t}"
+        : "=r"(h)
+        : "r"(q16), "l"(s2));
+    return h;
+}
+
+}  // namespace ebx

@@ -51,6 +51,7 @@ struct DecodeArgs {
     int kt;
     int groups;       // row groups (N padded to 16) / 16
     uint32_t magic;   // 0x4B000000 (2^23), passed in so the compiler keeps it in a register
+    uint32_t magic_plane;  // 0x64646464 (fp16 upper bytes of 1024), likewise
     int stages;       // pipe kernel: ring depth (runtime, <= kMaxStages)
     int stage_bytes;  // pipe kernel: RG weight rounds + (min(M, 8 NT) + 1) activation rows
     XchgArgs xa;      // world > 0: fp32 partials go to the tensor-parallel exchange
@@ -220,6 +221,26 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(DecodeArgs a) {
         if (t + D - 1 < t1) issue(t + D - 1, (i + D - 1) % D);
         cp_async_commit();
 
+        if constexpr (plane_layout(B)) {
+            // plane layout: exact q pairs, then (fullPrecision) fp16_rn(fp32_rn(q * s))
+            uint32_t q16[16];
+            PlaneConsts pk;
+            pk.init(a.magic_plane);
+            plane_q16_all<B>(w, pk, q16);
+            if constexpr (!HW) {
+#pragma unroll
+                for (int p = 0; p < 16; ++p) q16[p] = q16_to_w16(q16[p], (p & 1) ? shi2 : slo2);
+            }
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+                const uint32_t af[4] = {q16[4 * s], q16[4 * s + 1], q16[4 * s + 2], q16[4 * s + 3]};
+#pragma unroll
+                for (int nb = 0; nb < NT; ++nb)
+                    mma_16816(acc[nb], af, xb[nb][(s >> 1) * 4 + (s & 1) * 2],
+                              xb[nb][(s >> 1) * 4 + (s & 1) * 2 + 1]);
+            }
+            continue;
+        }
 #pragma unroll
         for (int s = 0; s < 4; ++s) {
             uint32_t af[4];
@@ -338,6 +359,120 @@ __device__ __forceinline__ void pdl_trigger() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Consumer warp of the plane-layout decode (b = 8..12, one row group per CTA):
+// per ring round it takes TPW consecutive supertiles of the round's 8 * TPW,
+// decodes each lane's 32 codes to exact fp16 q pairs with byte permutes
+// (plane_q16_all) and issues mma.m16n8k16 against the staged activations.
+//   HW:   integer codes as operands, row scale applied after accumulation
+//         (the epilogue multiplies); fp16 holds every |q| <= 2047 exactly.
+//   !HW:  fp16_rn(fp32_rn(q * s)) operands (W16A16 semantics), from the same q.
+// Leaves the fp32 fragment sums of this warp in red[] for the CTA reduction.
+template <int B, bool HW, int NT, int TPW, class S>
+__device__ __forceinline__ void plane_consume(const DecodeArgs& a, uint8_t* smem, uint32_t full0,
+                                              uint32_t empty0, int rounds, int mrows, int wt,
+                                              int lane, float* red) {
+    const int g = blockIdx.x;
+    const bool grp_ok = g < a.groups;
+    const int r0 = lane >> 2;
+    const int c = lane & 3;
+    const int row_lo = g * kRowGroup + r0;
+    PlaneConsts pk;
+    pk.init(a.magic_plane);
+    uint64_t s2[2] = {0, 0};
+    if constexpr (!HW) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int row = row_lo + 8 * h;
+            const float sv = (grp_ok && row < a.N) ? a.scales[row] : 0.0f;
+            s2[h] = pack2f(sv, sv);
+        }
+    }
+    float acc[NT][4];
+#pragma unroll
+    for (int nb = 0; nb < NT; ++nb)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[nb][i] = 0.0f;
+    // this lane's operands in stage 0 (a round adds the stage offset `so`)
+    const int wb = wt * TPW * S::kTileBytes;
+    const int w16 = wb + lane * 16, w8 = wb + lane * 8, w4 = wb + lane * 4;
+    int xa[NT];
+#pragma unroll
+    for (int nb = 0; nb < NT; ++nb) {
+        const int tok = r0 + 8 * nb;
+        xa[nb] = S::kWBytes + (tok < mrows ? tok : mrows) * S::kXStride + wt * TPW * kKTile * 2 + 32 * c;
+    }
+    int rem = grp_ok ? a.kt - wt * TPW : 0;  // tiles of this warp's slot still ahead
+    int so = 0, st = 0;
+    uint32_t ph = 0;
+    for (int r = 0; r < rounds; ++r) {
+        if (!mbar_wait_bounded(full0 + 8u * uint32_t(st), ph)) {
+            if (lane == 0) atomicExch(&g_device_status, kDeviceTimeout);
+            break;
+        }
+#pragma unroll
+        for (int j = 0; j < TPW; ++j) {
+            const bool have = rem > j;
+            uint32_t w[B];
+            uint32_t xb[NT][8];
+            if (have) {
+                const int T0 = so + j * S::kTileBytes;
+#pragma unroll
+                for (int q = 0; q < B / 4; ++q) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(smem + w16 + T0 + q * 512);
+                    w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
+                }
+                if constexpr ((B & 2) != 0) {
+                    const uint2 v = *reinterpret_cast<const uint2*>(smem + w8 + T0 + (B / 4) * 512);
+                    w[4 * (B / 4)] = v.x;
+                    w[4 * (B / 4) + 1] = v.y;
+                }
+                if constexpr ((B & 1) != 0)
+                    w[B - 1] = *reinterpret_cast<const uint32_t*>(smem + w4 + T0 + (B / 4) * 512 +
+                                                                  ((B & 2) ? 256 : 0));
+#pragma unroll
+                for (int nb = 0; nb < NT; ++nb)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const uint4 v = *reinterpret_cast<const uint4*>(smem + xa[nb] + so +
+                                                                        j * kKTile * 2 + 16 * h);
+                        xb[nb][4 * h] = v.x; xb[nb][4 * h + 1] = v.y;
+                        xb[nb][4 * h + 2] = v.z; xb[nb][4 * h + 3] = v.w;
+                    }
+            }
+            if (j == TPW - 1) {  // every load of this stage has been issued
+                __syncwarp();
+                if (lane == 0) mbar_arrive(empty0 + 8u * uint32_t(st));
+            }
+            if (!have) continue;
+            uint32_t af[16];
+            plane_q16_all<B>(w, pk, af);
+            if constexpr (!HW) {
+#pragma unroll
+                for (int p = 0; p < 16; ++p) af[p] = q16_to_w16(af[p], s2[p & 1]);
+            }
+#pragma unroll
+            for (int s4 = 0; s4 < 4; ++s4) {
+                const uint32_t f[4] = {af[4 * s4], af[4 * s4 + 1], af[4 * s4 + 2], af[4 * s4 + 3]};
+#pragma unroll
+                for (int nb = 0; nb < NT; ++nb)
+                    mma_16816(acc[nb], f, xb[nb][(s4 >> 1) * 4 + (s4 & 1) * 2],
+                              xb[nb][(s4 >> 1) * 4 + (s4 & 1) * 2 + 1]);
+            }
+        }
+        rem -= S::kRound;
+        so += a.stage_bytes;
+        if (++st == a.stages) {
+            st = 0;
+            so = 0;
+            ph ^= 1u;
+        }
+    }
+#pragma unroll
+    for (int nb = 0; nb < NT; ++nb)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) red[((wt * NT + nb) * 32 + lane) * 4 + i] = acc[nb][i];
+}
+
 // RG row groups per CTA (consumer warp w: row group w / 8, tile 8r + w % 8);
 // every consumer of a round reads the same activation slice, so activation
 // traffic per weight falls by RG.  Requires K % 64 == 0 (the generic kernel
@@ -347,6 +482,9 @@ template <int B, bool HW, int NT, bool DIRECT, int RG, int MINB, int TPW>
 __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(DecodeArgs a) {
     using S = PipeStage<B, NT, RG, TPW>;
     constexpr int kConsumers = kWarps * RG;
+    // plane layout (b = 9..12), and b = 8's byte codes under integer semantics
+    constexpr bool kPlane = plane_layout(B) || (B == 8 && HW);
+    static_assert(!kPlane || RG == 1, "the plane decode takes one row group per CTA");
     extern __shared__ __align__(128) uint8_t smem[];
     const int D = a.stages;
     const int SB = a.stage_bytes;
@@ -426,6 +564,11 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
         if (!a.pdl_early) pdl_trigger();
     } else {
         // ---------------- consumer warps ----------------
+      if constexpr (kPlane) {
+        plane_consume<B, HW, NT, TPW, S>(a, smem, smem_u32(&full[0]), smem_u32(&empty[0]), rounds,
+                                         mrows, warp, lane, red);
+        if (!a.pdl_early) pdl_trigger();
+      } else {
         const int rgl = warp / kWarps;   // local row group
         const int wt = warp % kWarps;    // tile slot within the round
         const int g = blockIdx.x * RG + rgl;
@@ -435,7 +578,7 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
         const int row_lo = g * kRowGroup + r0;
         const uint32_t magic = a.magic;  // opaque: kept in a register, never re-materialised
         // b = 8..12 (fullPrecision): paired f32x2 decode with the row scale itself
-        constexpr bool kPaired = !HW && B >= 8 && B <= 12;
+        constexpr bool kPaired = !HW && B == 8;
         constexpr int kPB = kPaired ? B : 8;
         PairConsts<kPB> pk;
         uint64_t s2[2] = {0, 0};
@@ -603,6 +746,7 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
             for (int i = 0; i < 4; ++i)
                 red[(((rgl * kWarps + wt) * NT + nb) * 32 + lane) * 4 + i] = acc[nb][i];
         if (!a.pdl_early) pdl_trigger();
+      }
     }
     pdl_wait();  // outputs may alias the previous kernel's buffers
     __syncthreads();
@@ -827,7 +971,9 @@ cudaError_t launch_decode(const Matrix& m, const uint16_t* x, int64_t M, const u
     if (act && (xa || (m.rows % 16) != 0)) return cudaErrorInvalidValue;
     if (xa && M > 16) return cudaErrorInvalidValue;  // one launch = one exchange epoch
     const bool vecx = (m.cols % 64) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
-    const bool hw = m.exec_width < 16 && m.bits <= 8;
+    // integer-code semantics: exec width 4 / 8 (b <= 8, the reference's W4A16 / W8A16) and
+    // 12 (b <= 12: every |q| <= 2047 is an exact fp16 operand)
+    const bool hw = m.exec_width < 16 && m.bits <= 12;
     for (int64_t m0 = 0; m0 < M; m0 += 16) {
         DecodeArgs a;
         a.tiles = m.tiles;
@@ -845,6 +991,7 @@ cudaError_t launch_decode(const Matrix& m, const uint16_t* x, int64_t M, const u
         a.kt = int(m.kt);
         a.groups = int(m.groups);
         a.magic = 0x4B000000u;
+        a.magic_plane = 0x64646464u;
         const int groups = int(m.groups);
         cudaError_t e = cudaErrorInvalidValue;
         const bool v = vecx && ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0);
@@ -855,14 +1002,13 @@ cudaError_t launch_decode(const Matrix& m, const uint16_t* x, int64_t M, const u
         e = hw ? dispatch_nt<BB, true>(a, groups, v, m.direct_ok, s) : dispatch_nt<BB, false>(a, groups, v, m.direct_ok, s); \
         break;
             EBX_DEC_CASE(3) EBX_DEC_CASE(4) EBX_DEC_CASE(5) EBX_DEC_CASE(6) EBX_DEC_CASE(7)
-            EBX_DEC_CASE(8)
+            EBX_DEC_CASE(8) EBX_DEC_CASE(9) EBX_DEC_CASE(10) EBX_DEC_CASE(11) EBX_DEC_CASE(12)
 #undef EBX_DEC_CASE
 #define EBX_DEC_CASE_FULL(BB) \
     case BB:                  \
         e = dispatch_nt<BB, false>(a, groups, v, m.direct_ok, s); \
         break;
-            EBX_DEC_CASE_FULL(9) EBX_DEC_CASE_FULL(10) EBX_DEC_CASE_FULL(11)
-            EBX_DEC_CASE_FULL(12) EBX_DEC_CASE_FULL(13) EBX_DEC_CASE_FULL(14)
+            EBX_DEC_CASE_FULL(13) EBX_DEC_CASE_FULL(14)
             EBX_DEC_CASE_FULL(15) EBX_DEC_CASE_FULL(16)
 #undef EBX_DEC_CASE_FULL
             default:

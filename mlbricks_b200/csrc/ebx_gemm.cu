@@ -387,7 +387,7 @@ __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, ui
 // +1; rr odd -> row r0 + 8) -> exact fp16 pairs.
 // Paired-decode constants of a b = 8..12 code (a placeholder width otherwise).
 template <int B>
-using DgConsts = PairConsts<(B >= 8 && B <= 12) ? B : 8>;
+using DgConsts = PairConsts<8>;
 
 template <int B, bool HW>
 __device__ __forceinline__ void dg_decode(const uint32_t (&w)[B], const uint64_t (&s2)[2],
@@ -395,12 +395,22 @@ __device__ __forceinline__ void dg_decode(const uint32_t (&w)[B], const uint64_t
     if constexpr (B == kFp16Bits) {
 #pragma unroll
         for (int p = 0; p < 16; ++p) af[p] = w[p];
+    } else if constexpr (plane_layout(B) || (B == 8 && HW)) {
+        // plane layout (and b = 8's byte codes): exact q pairs by byte permutes;
+        // fullPrecision then rounds fp32_rn(q * s) once to fp16
+        PlaneConsts k;
+        k.init(0x64646464u);
+        plane_q16_all<B>(w, k, af);
+        if constexpr (!HW) {
+#pragma unroll
+            for (int p = 0; p < 16; ++p) af[p] = q16_to_w16(af[p], s2[p & 1]);
+        }
     } else if constexpr (HW) {
         const float nb = -(8388608.0f + float(qmax_for(B)));
         const uint64_t nb2 = pack2f(nb, nb);
 #pragma unroll
         for (int p = 0; p < 16; ++p) af[p] = codes2_to_half(code_magic<B>(w, 2 * p), code_magic<B>(w, 2 * p + 1), nb2);
-    } else if constexpr (B >= 8 && B <= 12) {
+    } else if constexpr (B == 8) {
         uint32_t lo[4], hi[4];
         dequant_steps<B, 0>(w, pk, s2, lo, hi);
 #pragma unroll
@@ -864,19 +874,19 @@ cudaError_t launch_dgemm(const Matrix& m, const uint16_t* x, int64_t M, const ui
     a.b_off = p.b_off;
     a.c_off = p.c_off;
     const unsigned grid = unsigned(((m.groups + kDgGroups - 1) / kDgGroups) * p.S);
-    const bool hw = m.exec_width < 16 && m.bits <= 8;
+    const bool hw = m.exec_width < 16 && m.bits <= 12;
     switch (m.bits) {
 #define EBX_DG_CASE(BB)                                                                  \
     case BB:                                                                             \
         return hw ? launch_dgemm_b<BB, true>(m, tx, a, grid, p.smem, dev, s)             \
                   : launch_dgemm_b<BB, false>(m, tx, a, grid, p.smem, dev, s);
         EBX_DG_CASE(3) EBX_DG_CASE(4) EBX_DG_CASE(5) EBX_DG_CASE(6) EBX_DG_CASE(7) EBX_DG_CASE(8)
+        EBX_DG_CASE(9) EBX_DG_CASE(10) EBX_DG_CASE(11) EBX_DG_CASE(12)
 #undef EBX_DG_CASE
 #define EBX_DG_CASE(BB) \
     case BB:            \
         return launch_dgemm_b<BB, false>(m, tx, a, grid, p.smem, dev, s);
-        EBX_DG_CASE(9) EBX_DG_CASE(10) EBX_DG_CASE(11) EBX_DG_CASE(12) EBX_DG_CASE(13)
-        EBX_DG_CASE(14) EBX_DG_CASE(15) EBX_DG_CASE(16)
+        EBX_DG_CASE(13) EBX_DG_CASE(14) EBX_DG_CASE(15) EBX_DG_CASE(16)
 #undef EBX_DG_CASE
         default:
             return cudaErrorInvalidValue;

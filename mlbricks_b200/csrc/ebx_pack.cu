@@ -67,10 +67,20 @@ __global__ void to_tiles_kernel(Src src, uint8_t* tiles, int bits, int64_t kt,
     uint32_t words[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) words[i] = 0;
+    const bool plane = plane_layout(bits);
     for (int j = 0; j < 32; ++j) {
         int r, k;
         code_position(lane, j, &r, &k);
         const uint32_t code = src(int(g * kRowGroup + r), int(t * kKTile + k));
+        if (plane) {
+            words[j >> 2] |= (code & 0xFFu) << (8 * (j & 3));
+            for (int hb = 0; hb < bits - 8; ++hb) {
+                int wi, bi;
+                plane_hi_bit(bits, j, hb, &wi, &bi);
+                words[wi] |= ((code >> (8 + hb)) & 1u) << bi;
+            }
+            continue;
+        }
         const int bit = j * bits;
         const int wi = bit >> 5, o = bit & 31;
         words[wi] |= code << o;
@@ -91,6 +101,18 @@ __device__ __forceinline__ uint32_t tile_code(const uint8_t* tiles, int bits, in
     const int lane = (rin & 7) * 4 + c;
     const int j = 8 * s + e;
     const uint8_t* base = tiles + (g * kt + t) * tile_bytes(bits);
+    if (plane_layout(bits)) {
+        uint32_t code =
+            (*reinterpret_cast<const uint32_t*>(base + word_offset(bits, lane, j >> 2)) >> (8 * (j & 3))) &
+            0xFFu;
+        for (int hb = 0; hb < bits - 8; ++hb) {
+            int wi, bi;
+            plane_hi_bit(bits, j, hb, &wi, &bi);
+            code |= ((*reinterpret_cast<const uint32_t*>(base + word_offset(bits, lane, wi)) >> bi) & 1u)
+                    << (8 + hb);
+        }
+        return code;
+    }
     const int bit = j * bits, wi = bit >> 5, o = bit & 31;
     uint64_t v = *reinterpret_cast<const uint32_t*>(base + word_offset(bits, lane, wi));
     if (o + bits > 32)
@@ -159,7 +181,19 @@ __global__ void materialize_kernel(const uint8_t* tiles, const float* scales, in
     if constexpr (B == kFp16Bits) {
 #pragma unroll
         for (int p = 0; p < 16; ++p) h[p] = w[p];
-    } else if constexpr (B >= 8 && B <= 12) {
+    } else if constexpr (plane_layout(B)) {
+        // plane layout: exact q pairs, then fp16_rn(fp32_rn(q * s)) (the decode kernel's
+        // arithmetic for the fullPrecision semantics)
+        const float sl = r0 < rows ? scales[r0] : 0.0f;
+        const float sh = r0 + 8 < rows ? scales[r0 + 8] : 0.0f;
+        PlaneConsts pk;
+        pk.init(0x64646464u);
+        uint32_t q16[16];
+        plane_q16_all<B>(w, pk, q16);
+        const uint64_t s2[2] = {pack2f(sl, sl), pack2f(sh, sh)};
+#pragma unroll
+        for (int p = 0; p < 16; ++p) h[p] = q16_to_w16(q16[p], s2[p & 1]);
+    } else if constexpr (B == 8) {
         // paired f32x2 decode (the decode kernel's arithmetic)
         const float sl = r0 < rows ? scales[r0] : 0.0f;
         const float sh = r0 + 8 < rows ? scales[r0 + 8] : 0.0f;

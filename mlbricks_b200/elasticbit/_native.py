@@ -147,10 +147,17 @@ _TUNE_CACHE: dict[str, int] = {}
 
 
 def _legal_widths(bits: int) -> tuple[int, ...]:
+    """Execution widths that represent `bits`-bit codes (cu:1174-1178 on the
+    reference).  4 and 8 are the reference's W4A16 / W8A16 integer-code
+    semantics; 12 is the same integer-code semantics for b <= 12, which the
+    B200 tensor cores execute exactly (every |q| <= 2047 is an fp16 operand);
+    16 is W16A16 over fp16(q * s)."""
     if bits <= 4:
         return (4, 8, 16)
     if bits <= 8:
         return (8, 16)
+    if bits <= 12:
+        return (12, 16)
     return (16,)
 
 
@@ -322,7 +329,7 @@ class RuntimeMatrix:
         if len(legal) == 1:
             return legal[0]
         props = torch.cuda.get_device_properties(self._device)
-        bucket = 4 if self._bits <= 4 else 8 if self._bits <= 8 else 16
+        bucket = 4 if self._bits <= 4 else 8 if self._bits <= 8 else 12 if self._bits <= 12 else 16
         key = f"{self._device}:{props.major}.{props.minor}:{self._rows}x{self._cols}:{bucket}"
         with _TUNE_LOCK:
             if key in _TUNE_CACHE:

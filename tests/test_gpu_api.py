@@ -42,7 +42,8 @@ def test_threshold_contract_and_policy_switch(cuda_ok, tmp_path):
     assert matrix.storageBits == analysis.selectedBits
     assert matrix.activateDType == "float16"
     assert matrix.executionPlanner == "cudaAutoTune"
-    legal = {4, 8, 16} if matrix.storageBits <= 4 else {8, 16} if matrix.storageBits <= 8 else {16}
+    b = matrix.storageBits
+    legal = {4, 8, 16} if b <= 4 else {8, 16} if b <= 8 else {12, 16} if b <= 12 else {16}
     assert matrix.executionWidth in legal
 
     x = calib[0]

@@ -3,9 +3,10 @@ ragged shapes, through the C ABI.
 
 Covers the 4096x4096, 14336x4096 and 4096x14336 decode shapes and ragged ones
 (N not a multiple of 16, one or two k-tiles per row) at every bit-width class
-of the decode kernel (b = 9..12 take the paired f32x2 dequantisation, b = 13
-the per-code one), the full and the integer (scale after accumulation)
-semantics, back-to-back launches of one matrix, first launches of matrices
+of the decode kernel (b = 9..12 are stored in the plane layout and decoded
+with byte permutes, b = 8 takes the paired f32x2 dequantisation under the full
+semantics, b = 13 the per-code one), the full and the integer (scale after
+accumulation; execution width 12 for b = 9..12) semantics, back-to-back launches of one matrix, first launches of matrices
 created on recycled device memory, CUDA-graph replays of launches that may
 overlap through programmatic dependent launch, and bit-identical repeats.
 
@@ -112,16 +113,31 @@ def test_decode_full_semantics(lib, rows, cols, bits, M):
     check(y, y32, ref)
 
 
-@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("bits", [4, 8, 9, 10, 11, 12])
 @pytest.mark.parametrize("M", [1, 6, 16])
 def test_decode_integer_semantics(lib, bits, M):
     rows, cols = 3000, 1024
     h, q, s = make(lib, rows, cols, bits, seed=bits + M)
-    _ebx.check(lib.ebx_matrix_set_execution_width(h.h, 8))
+    _ebx.check(lib.ebx_matrix_set_execution_width(h.h, 8 if bits <= 8 else 12))
     x = torch.randn((M, cols), device=dev()).half()
     y, y32 = run(lib, h, x, rows)
     torch.cuda.synchronize()
     ref = (x.double() @ q.double().t()) * s.double()
+    check(y, y32, ref)
+
+
+@pytest.mark.parametrize("rows,cols,bits", [sh for sh in SHAPES if 8 <= sh[2] <= 12])
+@pytest.mark.parametrize("M", [1, 2, 8, 16])
+def test_decode_integer_semantics_shapes(lib, rows, cols, bits, M):
+    """Execution width 12 (8 for b = 8) at the BASELINE and ragged shapes:
+    y = fp16(s * sum_k x_k q_k + bias), the reference's W8A16 arithmetic."""
+    h, q, s = make(lib, rows, cols, bits, seed=3 * rows + cols + bits)
+    _ebx.check(lib.ebx_matrix_set_execution_width(h.h, 8 if bits <= 8 else 12))
+    x = torch.randn((M, cols), device=dev()).half()
+    bias = (0.1 * torch.randn(rows, device=dev())).half()
+    y, y32 = run(lib, h, x, rows, bias)
+    torch.cuda.synchronize()
+    ref = (x.double() @ q.double().t()) * s.double() + bias.double()
     check(y, y32, ref)
 
 
@@ -222,12 +238,12 @@ def test_decode_gemm_full_semantics(lib, rows, cols, bits, M):
     assert st.value == 0
 
 
-@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("bits", [4, 8, 9, 10, 11, 12])
 @pytest.mark.parametrize("M", [24, 128])
 def test_decode_gemm_integer_semantics(lib, bits, M):
     rows, cols = 3000, 1024
     h, q, s = make(lib, rows, cols, bits, seed=bits + M)
-    _ebx.check(lib.ebx_matrix_set_execution_width(h.h, 8))
+    _ebx.check(lib.ebx_matrix_set_execution_width(h.h, 8 if bits <= 8 else 12))
     x = torch.randn((M, cols), device=dev()).half()
     y, y32 = run_ws(lib, h, x, rows)
     torch.cuda.synchronize()
