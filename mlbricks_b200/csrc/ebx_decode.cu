@@ -335,7 +335,7 @@ __device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity) {
 // copy of up to 512 halves per token row (lanes < M of the producer warp).  A
 // D-deep ring of rounds is guarded by per-stage full (TMA transaction count)
 // and empty (8 consumer-warp arrivals) mbarriers; every wait is bounded.
-constexpr int kMaxStages = 8;
+constexpr int kMaxStages = 16;
 
 // TPW: supertiles each consumer warp takes per round (one barrier wait, one
 // release and one loop trip per TPW tiles instead of per tile).
@@ -367,11 +367,13 @@ __device__ __forceinline__ void pdl_trigger() {
 //         (the epilogue multiplies); fp16 holds every |q| <= 2047 exactly.
 //   !HW:  fp16_rn(fp32_rn(q * s)) operands (W16A16 semantics), from the same q.
 // Leaves the fp32 fragment sums of this warp in red[] for the CTA reduction.
-template <int B, bool HW, int NT, int TPW, class S>
+template <int B, bool HW, int NT, int TPW, int RG, bool XG, class S>
 __device__ __forceinline__ void plane_consume(const DecodeArgs& a, uint8_t* smem, uint32_t full0,
-                                              uint32_t empty0, int rounds, int mrows, int wt,
+                                              uint32_t empty0, int rounds, int mrows, int warp,
                                               int lane, float* red) {
-    const int g = blockIdx.x;
+    const int rgl = warp / kWarps;  // local row group (RG > 1: the groups share each activation stage)
+    const int wt = warp % kWarps;   // tile slot within the round
+    const int g = blockIdx.x * RG + rgl;
     const bool grp_ok = g < a.groups;
     const int r0 = lane >> 2;
     const int c = lane & 3;
@@ -393,18 +395,60 @@ __device__ __forceinline__ void plane_consume(const DecodeArgs& a, uint8_t* smem
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[nb][i] = 0.0f;
     // this lane's operands in stage 0 (a round adds the stage offset `so`)
-    const int wb = wt * TPW * S::kTileBytes;
+    const int wb = rgl * S::kWBytes + wt * TPW * S::kTileBytes;
     const int w16 = wb + lane * 16, w8 = wb + lane * 8, w4 = wb + lane * 4;
     int xa[NT];
 #pragma unroll
     for (int nb = 0; nb < NT; ++nb) {
         const int tok = r0 + 8 * nb;
-        xa[nb] = S::kWBytes + (tok < mrows ? tok : mrows) * S::kXStride + wt * TPW * kKTile * 2 + 32 * c;
+        xa[nb] = RG * S::kWBytes + (tok < mrows ? tok : mrows) * S::kXStride + wt * TPW * kKTile * 2 +
+                 32 * c;
     }
     int rem = grp_ok ? a.kt - wt * TPW : 0;  // tiles of this warp's slot still ahead
+    const int rem0 = rem;
+    // XG: activations straight from global memory (L2) into registers, one round
+    // ahead, instead of through the shared-memory ring (which then holds weights only)
+    uint32_t xn[XG ? TPW : 1][NT][8];
+    const uint16_t* xrow[NT];
+    auto xload = [&](int r) {
+#pragma unroll
+        for (int j = 0; j < TPW; ++j)
+#pragma unroll
+            for (int nb = 0; nb < NT; ++nb) {
+                const bool ok = (r0 + 8 * nb) < a.M && (rem0 - r * S::kRound) > j;
+                uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0;
+                if (ok) {
+                    const uint4* p = reinterpret_cast<const uint4*>(
+                        xrow[nb] + (size_t(r) * S::kRound + j) * kKTile);
+                    v0 = __ldg(p);
+                    v1 = __ldg(p + 1);
+                }
+                xn[j][nb][0] = v0.x; xn[j][nb][1] = v0.y; xn[j][nb][2] = v0.z; xn[j][nb][3] = v0.w;
+                xn[j][nb][4] = v1.x; xn[j][nb][5] = v1.y; xn[j][nb][6] = v1.z; xn[j][nb][7] = v1.w;
+            }
+    };
+    if constexpr (XG) {
+#pragma unroll
+        for (int nb = 0; nb < NT; ++nb) {
+            const int tok = r0 + 8 * nb;
+            xrow[nb] = a.x + size_t(tok < a.M ? tok : 0) * a.K + size_t(wt) * TPW * kKTile + 16 * c;
+        }
+        pdl_wait();  // activations may be written by the previous kernel
+        xload(0);
+    }
     int so = 0, st = 0;
     uint32_t ph = 0;
     for (int r = 0; r < rounds; ++r) {
+        uint32_t xc[XG ? TPW : 1][NT][8];
+        if constexpr (XG) {
+#pragma unroll
+            for (int j = 0; j < TPW; ++j)
+#pragma unroll
+                for (int nb = 0; nb < NT; ++nb)
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) xc[j][nb][e] = xn[j][nb][e];
+            if (r + 1 < rounds) xload(r + 1);
+        }
         if (!mbar_wait_bounded(full0 + 8u * uint32_t(st), ph)) {
             if (lane == 0) atomicExch(&g_device_status, kDeviceTimeout);
             break;
@@ -429,15 +473,22 @@ __device__ __forceinline__ void plane_consume(const DecodeArgs& a, uint8_t* smem
                 if constexpr ((B & 1) != 0)
                     w[B - 1] = *reinterpret_cast<const uint32_t*>(smem + w4 + T0 + (B / 4) * 512 +
                                                                   ((B & 2) ? 256 : 0));
+                if constexpr (XG) {
 #pragma unroll
-                for (int nb = 0; nb < NT; ++nb)
+                    for (int nb = 0; nb < NT; ++nb)
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const uint4 v = *reinterpret_cast<const uint4*>(smem + xa[nb] + so +
-                                                                        j * kKTile * 2 + 16 * h);
-                        xb[nb][4 * h] = v.x; xb[nb][4 * h + 1] = v.y;
-                        xb[nb][4 * h + 2] = v.z; xb[nb][4 * h + 3] = v.w;
-                    }
+                        for (int e = 0; e < 8; ++e) xb[nb][e] = xc[XG ? j : 0][nb][e];
+                } else {
+#pragma unroll
+                    for (int nb = 0; nb < NT; ++nb)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const uint4 v = *reinterpret_cast<const uint4*>(smem + xa[nb] + so +
+                                                                            j * kKTile * 2 + 16 * h);
+                            xb[nb][4 * h] = v.x; xb[nb][4 * h + 1] = v.y;
+                            xb[nb][4 * h + 2] = v.z; xb[nb][4 * h + 3] = v.w;
+                        }
+                }
             }
             if (j == TPW - 1) {  // every load of this stage has been issued
                 __syncwarp();
@@ -470,7 +521,7 @@ __device__ __forceinline__ void plane_consume(const DecodeArgs& a, uint8_t* smem
 #pragma unroll
     for (int nb = 0; nb < NT; ++nb)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) red[((wt * NT + nb) * 32 + lane) * 4 + i] = acc[nb][i];
+        for (int i = 0; i < 4; ++i) red[(((rgl * kWarps + wt) * NT + nb) * 32 + lane) * 4 + i] = acc[nb][i];
 }
 
 // RG row groups per CTA (consumer warp w: row group w / 8, tile 8r + w % 8);
@@ -478,13 +529,12 @@ __device__ __forceinline__ void plane_consume(const DecodeArgs& a, uint8_t* smem
 // traffic per weight falls by RG.  Requires K % 64 == 0 (the generic kernel
 // covers the rest); activation rows of tokens >= M are zeroed once and never
 // written by the copy engine, so the fragment loads need no predicates.
-template <int B, bool HW, int NT, bool DIRECT, int RG, int MINB, int TPW>
+template <int B, bool HW, int NT, bool DIRECT, int RG, int MINB, int TPW, bool XG = false>
 __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(DecodeArgs a) {
     using S = PipeStage<B, NT, RG, TPW>;
     constexpr int kConsumers = kWarps * RG;
     // plane layout (b = 9..12), and b = 8's byte codes under integer semantics
     constexpr bool kPlane = plane_layout(B) || (B == 8 && HW);
-    static_assert(!kPlane || RG == 1, "the plane decode takes one row group per CTA");
     extern __shared__ __align__(128) uint8_t smem[];
     const int D = a.stages;
     const int SB = a.stage_bytes;
@@ -505,10 +555,11 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
     }
     // zero row (index mrows) of every stage, never written by the copy engine:
     // lanes whose token is >= M read it
-    for (int i = threadIdx.x; i < D * (S::kXStride / 16); i += blockDim.x)
-        *reinterpret_cast<uint4*>(smem + (i / (S::kXStride / 16)) * SB + RG * S::kWBytes +
-                                  mrows * S::kXStride + (i % (S::kXStride / 16)) * 16) =
-            make_uint4(0, 0, 0, 0);
+    if constexpr (!XG)
+        for (int i = threadIdx.x; i < D * (S::kXStride / 16); i += blockDim.x)
+            *reinterpret_cast<uint4*>(smem + (i / (S::kXStride / 16)) * SB + RG * S::kWBytes +
+                                      mrows * S::kXStride + (i % (S::kXStride / 16)) * 16) =
+                make_uint4(0, 0, 0, 0);
     fence_proxy_async_smem();
     __syncthreads();
 
@@ -527,7 +578,8 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
             uint8_t* dst = smem + st * SB;
             const uint32_t bar = smem_u32(&full[st]);
             if (lane == 0) {
-                mbar_expect_tx(bar, uint32_t(ngroups * ntile * S::kTileBytes) + xbytes * uint32_t(mrows));
+                mbar_expect_tx(bar, uint32_t(ngroups * ntile * S::kTileBytes) +
+                                        (XG ? 0u : xbytes * uint32_t(mrows)));
 #pragma unroll
                 for (int rg = 0; rg < RG; ++rg) {
                     const int g = blockIdx.x * RG + rg;
@@ -540,7 +592,7 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
         };
         auto acts = [&](int r, int st) {
             const int ntile = min(S::kRound, a.kt - r * S::kRound);
-            if (lane < mrows)
+            if (!XG && lane < mrows)
                 bulk_g2s(smem_u32(smem + st * SB + RG * S::kWBytes + lane * S::kXStride),
                          a.x + size_t(lane) * a.K + size_t(r) * S::kRound * kKTile,
                          uint32_t(ntile * kKTile * 2), smem_u32(&full[st]));
@@ -565,8 +617,8 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
     } else {
         // ---------------- consumer warps ----------------
       if constexpr (kPlane) {
-        plane_consume<B, HW, NT, TPW, S>(a, smem, smem_u32(&full[0]), smem_u32(&empty[0]), rounds,
-                                         mrows, warp, lane, red);
+        plane_consume<B, HW, NT, TPW, RG, XG, S>(a, smem, smem_u32(&full[0]), smem_u32(&empty[0]),
+                                                 rounds, mrows, warp, lane, red);
         if (!a.pdl_early) pdl_trigger();
       } else {
         const int rgl = warp / kWarps;   // local row group
@@ -878,22 +930,23 @@ cudaError_t launch_one(DecodeArgs& a, int groups, cudaStream_t s) {
     return launch_maybe_xchg(kern, a, unsigned(groups), kThreads, smem, s);
 }
 
-template <int B, bool HW, int NT, bool DIRECT, int RG, int TPW, int MINB = (RG == 1 ? 3 : 1)>
+template <int B, bool HW, int NT, bool DIRECT, int RG, int TPW, int MINB = (RG == 1 ? 3 : 1),
+          bool XG = false>
 cudaError_t launch_pipe(DecodeArgs& a, int groups, cudaStream_t s) {
     using S = PipeStage<B, NT, RG, TPW>;
     // MINB CTAs per SM share its shared memory (three: 27 warps; two: 18; RG == 2:
     // one CTA of 17 warps).  The ring is as deep as that budget allows for this M
     // (2..kMaxStages stages).
-    constexpr int kBudget = MINB == 3 ? 74 * 1024 : (MINB == 2 ? 110 * 1024 : 215 * 1024);
+    constexpr int kBudget = MINB >= 4 ? 54 * 1024 : MINB == 3 ? 74 * 1024 : (MINB == 2 ? 110 * 1024 : 215 * 1024);
     constexpr int kFixed = 2 * kMaxStages * 8 + S::kRedBytes + 16;
     const int mrows = a.M < NT * 8 ? a.M : NT * 8;
-    a.stage_bytes = S::bytes(mrows);
+    a.stage_bytes = XG ? RG * S::kWBytes : S::bytes(mrows);
     int D = (kBudget - kFixed) / a.stage_bytes;
     D = D > kMaxStages ? kMaxStages : D;
     if (D < 2) return cudaErrorInvalidConfiguration;  // dispatch keeps every case >= 2 stages
     a.stages = D;
     const int smem = D * a.stage_bytes + kFixed;
-    auto kern = decode_pipe_kernel<B, HW, NT, DIRECT, RG, MINB, TPW>;
+    auto kern = decode_pipe_kernel<B, HW, NT, DIRECT, RG, MINB, TPW, XG>;
     static std::atomic<uint64_t> configured{0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -910,6 +963,38 @@ cudaError_t launch_pipe(DecodeArgs& a, int groups, cudaStream_t s) {
 
 template <int B, bool HW>
 cudaError_t dispatch_nt(DecodeArgs& a, int groups, bool pipe, bool direct, cudaStream_t s) {
+    constexpr bool kPlane = plane_layout(B) || (B == 8 && HW);
+    if constexpr (kPlane) {
+        if (pipe) {
+            // Launch shapes of the plane decode, measured on the BASELINE decode shapes
+            // (b = 10, 11; GB/s of the sweep's graph replay):
+            //  * grids that fit two CTAs per SM in one wave with K <= 8192 (4096 x 4096):
+            //    two CTAs per SM, two supertiles per warp and round, up to M = 8;
+            //  * 896-row-group grids (N = 14336): three CTAs per SM with two supertiles
+            //    per warp and round at M = 1, four CTAs with one supertile for 1 < M <= 8
+            //    (4.41 vs 4.26 TB/s at M = 2, 3.98 vs 3.60 at M = 8);
+            //  * K = 14336 (few, long CTAs): three CTAs per SM at M <= 4, two at M <= 8;
+            //  * 8 < M <= 16: two row groups per CTA sharing each activation stage, which
+            //    halves the activation bytes staged per weight byte (1 CTA per SM with a
+            //    deep ring, or two CTAs with one supertile per warp for the 896-group
+            //    grid): 2.36 -> 2.92, 2.71 -> 2.92, 2.57 -> 3.39 TB/s.
+            const bool two_per_sm = groups <= 2 * sm_count() && a.kt <= 128;
+            if (a.M <= 8) {
+                if (two_per_sm) return launch_pipe<B, HW, 1, false, 1, 2, 2>(a, groups, s);
+                if (a.kt > 128)
+                    return a.M <= 4 ? launch_pipe<B, HW, 1, false, 1, 2, 3>(a, groups, s)
+                                    : launch_pipe<B, HW, 1, false, 1, 2, 2>(a, groups, s);
+                if (a.M == 1) return launch_pipe<B, HW, 1, false, 1, 2, 3>(a, groups, s);
+                // (the fullPrecision operands need more registers than four CTAs per SM leave)
+                if (!HW)
+                    return a.M <= 4 ? launch_pipe<B, HW, 1, false, 1, 2, 3>(a, groups, s)
+                                    : launch_pipe<B, HW, 1, false, 1, 2, 2>(a, groups, s);
+                return launch_pipe<B, HW, 1, false, 1, 1, 4>(a, groups, s);
+            }
+            if (HW && groups > 2 * sm_count()) return launch_pipe<B, HW, 2, false, 2, 1, 2>(a, groups, s);
+            return launch_pipe<B, HW, 2, false, 2, 2, 1>(a, groups, s);
+        }
+    }
     if (pipe) {
         // M <= 4 and b <= 12: two supertiles per warp per round (a stage of 16 supertiles
         // and up to 5 activation rows still leaves >= 2 stages in the 74 KB budget);
