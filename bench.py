@@ -140,8 +140,10 @@ def baseline_weights_gpu(N: int, K: int, seed: int, device):
     return w.half()
 
 
-def build_matrices(device, seed0: int = 0):
-    """Compress the 9 (shape, threshold) matrices with the ElasticBit analyzer."""
+def build_matrices(device, seed0: int = 0, keep_codes: bool = False):
+    """Compress the 9 (shape, threshold) matrices with the ElasticBit analyzer
+    (keep_codes: also keep the selected codes and scales on the host, for the
+    reference leg)."""
     import numpy as np
     import torch
 
@@ -158,7 +160,10 @@ def build_matrices(device, seed0: int = 0):
                                                          decodePolicy="hardwareNative")
             else:
                 m = RuntimeMatrix._compressSelected(w16.float(), bits, thr, err)
-            out.append({"K": K, "N": N, "threshold": thr, "bits": bits, "matrix": m})
+            e = {"K": K, "N": N, "threshold": thr, "bits": bits, "matrix": m}
+            if keep_codes and bits <= 15:
+                e.update(codes=codes.cpu().numpy(), scales=scales.cpu().numpy(), error=err)
+            out.append(e)
             del codes, scales
         del w16
         torch.cuda.empty_cache()
@@ -185,7 +190,8 @@ def run_gpu(args) -> None:
                                 device_id=device)
     lib = _ebx.load()
 
-    mats = build_matrices(device)
+    ref_leg = rank == 0 and world == 1 and not args.no_reference_gpu
+    mats = build_matrices(device, keep_codes=ref_leg)
     torch.cuda.synchronize()
 
     # inputs / outputs (device) for every (M, matrix)
@@ -280,6 +286,10 @@ def run_gpu(args) -> None:
     # e2e through the public API with pinned host buffers
     e2e = run_e2e(mats, device, args)
 
+    # the reference's own CUDA path on this GPU, same matrices and per-M mix (after our
+    # timed region; rank 0 of a single-GPU run)
+    reference_gpu = reference_gpu_leg(mats, device, args, per_m) if ref_leg else None
+
     # config 5: tensor-parallel 8B-shaped linear stack over all ranks
     mat_info = [{"K": e["K"], "N": e["N"], "threshold": e["threshold"], "bits": e["bits"]}
                 for e in mats]
@@ -322,6 +332,7 @@ def run_gpu(args) -> None:
             "peak_source": pk["source"], "kernel": "ebx decode_pipe_kernel (M<=16)",
         },
         "e2e": e2e,
+        "reference_gpu": reference_gpu,
         "prefill": prefill,
         "tp_stack": tp_stack,
         "bolt_decoder": bolt,
@@ -336,6 +347,125 @@ def run_gpu(args) -> None:
         dist.destroy_process_group()
     if rank == 0:
         emit(result)
+
+
+def _load_reference_runtime():
+    """The reference's compiled ElasticBit runtime (oracle/_ref/_C.so, built from the
+    reference sources by oracle/build.py), or None when it was not built."""
+    import importlib.util
+
+    import torch  # noqa: F401  (libc10 / libtorch for the extension)
+
+    so = ROOT / "oracle" / "_ref" / "_C.so"
+    if not so.exists():
+        return None
+    spec = importlib.util.spec_from_file_location("_C", so)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def reference_gpu_leg(mats, device, args, ours_per_m) -> dict:
+    """The reference's stock forward (core.py:446-471) on the same nine matrices and
+    the same M mix, on this GPU: M = 1 through RuntimeMatrix.forwardTorch (its
+    FastWarp GEMV, cu:902-931 / 614-648) and M > 1 through F.linear over
+    _materializeTorch() (the W16 execution copy, cu:982-1022), each matrix built by
+    the reference's own _compressSelectedCodes with the analyzer's codes and its
+    default hardwareNative policy.  Timed like our sweep: one CUDA graph per M,
+    CUDA events on the launching stream; GB/s of the same algorithmic bytes."""
+    import torch
+    import torch.nn.functional as F
+
+    ref = _load_reference_runtime()
+    if ref is None:
+        return {"unavailable": "oracle/_ref/_C.so was not built"}
+    rms = []
+    for e in mats:
+        if "codes" not in e:
+            return {"unavailable": "a matrix kept its FP16 weight (16-bit fallback)"}
+        rms.append((e, ref.RuntimeMatrix._compressSelectedCodes(
+            e["codes"], e["scales"], e["bits"], e["threshold"], e["error"], "hardwareNative")))
+        e.pop("codes")
+        e.pop("scales")
+    xs = {M: {K: torch.randn((M, K), device=device, dtype=torch.float16) for K in {4096, 14336}}
+          for M in MS}
+    w16 = {id(e): rm._materializeTorch() for e, rm in rms}
+
+    def run(M):
+        for e, rm in rms:
+            if M == 1:
+                rm.forwardTorch(xs[1][e["K"]].view(-1))
+            else:
+                F.linear(xs[M][e["K"]], w16[id(e)])
+
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        for M in MS:
+            run(M)
+    stream.synchronize()
+    graphs, mode = {}, "CUDA graph per M"
+    try:
+        for M in MS:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                run(M)
+            graphs[M] = g
+    except Exception as exc:  # capture refused: time eager launches instead
+        graphs, mode = {}, f"eager launches (graph capture failed: {type(exc).__name__})"
+    steps = max(3, min(args.steps, 20))
+    per_m, tot_b, tot_ms = {}, 0.0, 0.0
+    for M in MS:
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                graphs[M].replay() if graphs else run(M)
+            a.record(stream)
+            for _ in range(steps):
+                graphs[M].replay() if graphs else run(M)
+            b.record(stream)
+        b.synchronize()
+        ms = a.elapsed_time(b)
+        byts = sum(algorithmic_bytes(e["N"], e["K"], e["bits"], M) for e, _ in rms) * steps
+        per_m[str(M)] = round(byts / (ms * 1e-3) / 1e9, 1)
+        tot_b += byts
+        tot_ms += ms
+    del graphs
+    # prefill (config 3): the reference's M > 1 route is F.linear on the W16 copy
+    pre, flops, pre_ms = [], 0.0, 0.0
+    for e, rm in rms:
+        if e["threshold"] != 0.01:
+            continue
+        for M in PREFILL_MS:
+            x = torch.randn((M, e["K"]), device=device, dtype=torch.float16)
+            for _ in range(2):
+                F.linear(x, w16[id(e)])
+            times = []
+            for _ in range(5):
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record()
+                F.linear(x, w16[id(e)])
+                b.record()
+                b.synchronize()
+                times.append(a.elapsed_time(b))
+            t = statistics.median(times)
+            pre.append({"M": M, "K": e["K"], "N": e["N"], "ms": round(t, 4),
+                        "TFLOPs": round(2.0 * M * e["N"] * e["K"] / (t * 1e-3) / 1e12, 1)})
+            if M == 4096:
+                flops += 2.0 * M * e["N"] * e["K"]
+                pre_ms += t
+    del w16, rms
+    torch.cuda.empty_cache()
+    value = tot_b / (tot_ms * 1e-3) / 1e9
+    return {"value": round(value, 1), "unit": "GB/s", "per_M_GBps": per_m,
+            "M4096_TFLOPs": round(flops / (pre_ms * 1e-3) / 1e12, 1) if pre_ms else None,
+            "prefill_cases": pre,
+            "ebx_over_reference_per_M": {M: round(ours_per_m[M] / per_m[M], 2) for M in per_m},
+            "timing": mode,
+            "route": "reference RuntimeMatrix (oracle/_ref/_C.so, built from the reference "
+                     "sources): forwardTorch (FastWarp) at M = 1, F.linear over "
+                     "_materializeTorch() (cuBLAS on the FP16 execution copy) at M > 1"}
 
 
 PREFILL_MS = [256, 1024, 4096]
@@ -390,28 +520,34 @@ def build_stack(device, world: int, rank: int, collectives, exchange=None):
                 pending[name] = (q, sc)
                 if len(pending) == 2:  # one launch: gate/up interleaved, SwiGLU in the epilogue
                     layer["swiglu"] = tp.build_column_swiglu(pending["gate"], pending["up"],
-                                                             bits_of["gate"], world, rank)
+                                                             bits_of["gate"], world, rank,
+                                                             integer=True)
                     pending.clear()
                 continue
             layer[name] = tp.build_sharded(q, sc, bits_of[name], mode, world, rank,
                                            collectives=collectives,
-                                           input_is_local=(mode == "row"), exchange=exchange)
+                                           input_is_local=(mode == "row"), exchange=exchange,
+                                           integer=True)
             del q, sc
         layers.append(layer)
     name, K, N, mode = STACK_HEAD
     w = baseline_weights_gpu(N, K, 99_999, device)
     q, sc = quantize_rows(w, bits_of[name])
     del w
-    head = tp.build_sharded(q, sc, bits_of[name], mode, world, rank, collectives=collectives)
+    head = tp.build_sharded(q, sc, bits_of[name], mode, world, rank, collectives=collectives,
+                            integer=True)
     del q, sc
     torch.cuda.empty_cache()
     return layers, head, bits_of
 
 
-def stack_step(layers, head, h, world: int):
+def stack_step(layers, head, h, world: int, collectives=None):
     """One forward of the linear stack on M rows (attention replaced by the q slice of
-    QKV; SiLU(gate) * up between the MLP projections); returns local logits."""
+    QKV; SiLU(gate) * up between the MLP projections); returns the greedy next-token
+    ids (argmax over the column-parallel logits, one all-gather of per-rank maxima)."""
     import torch
+
+    from mlbricks_b200.elasticbit import tensor_parallel as tp
 
     for L in layers:
         qkv = L["qkv"](h)                               # [M, 6144 / W] local
@@ -422,46 +558,32 @@ def stack_step(layers, head, h, world: int):
         else:
             act = torch.nn.functional.silu(L["gate"](h)) * L["up"](h)
         h = L["down"](act)                              # all-reduce -> [M, 4096]
-    return head(h)
+    return tp.greedy_argmax(head(h), head.bounds[0], collectives)
 
 
-def run_tp_stack(args, world: int, rank: int, device) -> dict:
+def _time_stack(layers, head, world: int, device, steps: int, coll) -> dict:
+    """Decode tok/s (one CUDA graph per step, greedy ids out) at M = 1, 16, 64 and the
+    2048-token prefill tok/s; max over ranks when world > 1."""
     import torch
     import torch.distributed as dist
 
-    from mlbricks_b200.elasticbit import tensor_parallel as tp
-
-    coll = tp.Collectives.from_group() if world > 1 else None
-    # decode batches <= 16: row-parallel layers all-reduce through the libebx exchange
-    # (fp32 partials stored into every rank's region over NVLink); larger M: NCCL
-    exchange = (tp.Exchange.from_group(16, 4096)
-                if world > 1 and not getattr(args, "nccl_only", False) else None)
-    layers, head, bits_of = build_stack(device, world, rank, coll, exchange)
-    out = {"workload": "config5: 32 x (QKV 4096->6144 col, O 4096->4096 row, gate/up 4096->14336 "
-                       "col, down 14336->4096 row) + lm_head 4096->128256 col, threshold 0.01; "
-                       f"Megatron TP over {world} GPU(s); row-parallel all-reduce: "
-                       + ("libebx exchange (M<=16), NCCL fp32 (M>16)" if exchange else
-                          "NCCL fp32" if world > 1 else "none") +
-                       "; gate/up interleaved per rank with SwiGLU fused into the decode epilogue (M<=16); "
-                       "one CUDA graph per decode step",
-           "bits": bits_of, "decode_tok_s": {}}
+    out = {"decode_tok_s": {}}
     stream = torch.cuda.Stream(device)
     for M in (1, 16, 64):
         h0 = torch.randn((M, 4096), device=device, dtype=torch.float16)
         with torch.cuda.stream(stream):
             for _ in range(2):
-                logits = stack_step(layers, head, h0, world)
+                ids = stack_step(layers, head, h0, world, coll)
         stream.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
-            logits = stack_step(layers, head, h0, world)
+            ids = stack_step(layers, head, h0, world, coll)
         with torch.cuda.stream(stream):
             for _ in range(2):
                 g.replay()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-        steps = max(3, min(args.steps, 20))
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):  # replay runs on the current stream
@@ -474,24 +596,139 @@ def run_tp_stack(args, world: int, rank: int, device) -> dict:
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         out["decode_tok_s"][str(M)] = round(M * steps / (float(t.item()) * 1e-3), 1)
-        del g, logits
-    # 2048-token prefill (tensor-core GEMM route)
+        del g, ids
     x = torch.randn((2048, 4096), device=device, dtype=torch.float16)
     with torch.cuda.stream(stream):
-        stack_step(layers, head, x, world)
+        stack_step(layers, head, x, world, coll)
         stream.synchronize()
         if world > 1:
             dist.barrier()
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        stack_step(layers, head, x, world)
+        stack_step(layers, head, x, world, coll)
         b.record(stream)
     b.synchronize()
     t = torch.tensor([a.elapsed_time(b)], device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     out["prefill2048_tok_s"] = round(2048 / (float(t.item()) * 1e-3), 1)
+    return out
+
+
+def tp_parity(layers, head, bits_of, world: int, rank: int, device, coll) -> dict:
+    """Sharded vs unsharded outputs of one layer of every kind (column QKV, row O,
+    fused SwiGLU gate/up, row down, column lm_head and its greedy argmax) on this
+    rank's GPU, at M = 1, 16 (exchange route for row layers) and 64 (NCCL route).
+    The unsharded matrices are rebuilt from the same seeds and run with the same
+    integer-code semantics.  Bar: |y - ref| <= max(2e-3, one fp16 ulp of ref)
+    elementwise and relative L2 <= 1e-3; every rank's result is reduced (max)."""
+    import torch
+    import torch.distributed as dist
+
+    from mlbricks_b200.elasticbit import tensor_parallel as tp
+
+    def full(name, seed):
+        K, N = {m[0]: (m[1], m[2]) for m in STACK_MATS + [STACK_HEAD]}[name]
+        w = baseline_weights_gpu(N, K, seed, device)
+        q, sc = quantize_rows(w, bits_of[name])
+        del w
+        return tp.build_sharded(q, sc, bits_of[name], "column", 1, 0, integer=True).matrix._native
+
+    ref_m = {name: full(name, 10_000 + mi) for mi, (name, _, _, _) in enumerate(STACK_MATS)}
+    ref_m["lm_head"] = full("lm_head", 99_999)
+    L0 = layers[0]
+    worst = {"max_abs": 0.0, "rel_l2": 0.0, "violations": 0, "argmax_mismatch": 0}
+
+    def cmp(y, ref):
+        y, ref = y.float(), ref.float()
+        d = (y - ref).abs()
+        tol = torch.clamp(torch.abs(ref.half().float()) * 2.0 ** -10, min=2e-3)
+        worst["max_abs"] = max(worst["max_abs"], float(d.max()))
+        worst["rel_l2"] = max(worst["rel_l2"], float(d.norm() / ref.norm().clamp_min(1e-30)))
+        worst["violations"] += int((d > tol).sum())
+
+    g = torch.Generator(device=device)
+    for M in (1, 16, 64):
+        g.manual_seed(123 + M)
+        x = torch.randn((M, 4096), device=device, generator=g).half()
+        a = torch.randn((M, 4096), device=device, generator=g).half()
+        d = torch.randn((M, 14336), device=device, generator=g).half()
+        lo, hi = L0["qkv"].bounds
+        cmp(L0["qkv"](x), ref_m["qkv"].linear(x)[:, lo:hi])
+        lo, hi = L0["o"].bounds
+        cmp(L0["o"](a[:, lo:hi].contiguous()), ref_m["o"].linear(a))
+        if "swiglu" in L0:
+            lo, hi = tp.shard_bounds(14336, world, rank, 16)
+            gate = ref_m["gate"].linear(x, None, out32=True)[1]
+            up = ref_m["up"].linear(x, None, out32=True)[1]
+            cmp(L0["swiglu"](x), (torch.nn.functional.silu(gate) * up).half()[:, lo:hi])
+        lo, hi = L0["down"].bounds
+        cmp(L0["down"](d[:, lo:hi].contiguous()), ref_m["down"].linear(d))
+        lo, hi = head.bounds
+        full_logits = ref_m["lm_head"].linear(x)
+        local = head(x)
+        cmp(local, full_logits[:, lo:hi])
+        ids = tp.greedy_argmax(local, lo, coll)
+        worst["argmax_mismatch"] += int((ids != full_logits.float().argmax(dim=-1)).sum())
+    torch.cuda.synchronize()
+    t = torch.tensor([worst["max_abs"], worst["rel_l2"], worst["violations"],
+                      worst["argmax_mismatch"]], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    del ref_m
+    torch.cuda.empty_cache()
+    return {"max_abs": round(float(t[0]), 6), "rel_l2": float(f"{float(t[1]):.3e}"),
+            "elements_over_tol": int(t[2]), "argmax_mismatch": int(t[3]),
+            "ok": bool(t[1] <= 1e-3 and t[2] == 0 and t[3] == 0), "ranks": world,
+            "M": [1, 16, 64],
+            "layers": "qkv (column), o (row; exchange at M <= 16, NCCL at 64), gate/up SwiGLU "
+                      "(column, fused), down (row), lm_head (column) + distributed greedy argmax",
+            "bar": "|y - ref| <= max(2e-3, fp16 ulp) elementwise, relative L2 <= 1e-3; "
+                   "ref = the unsharded matrix on the same GPU"}
+
+
+def run_tp_stack(args, world: int, rank: int, device) -> dict:
+    import torch
+    import torch.distributed as dist
+
+    from mlbricks_b200.elasticbit import tensor_parallel as tp
+
+    steps = max(3, min(args.steps, 20))
+    unsharded = None
+    if world > 1:
+        # the same stack unsharded on every rank's own GPU (all ranks at once, so no
+        # rank waits on another), the N = 1 point of this run's efficiency
+        layers1, head1, _ = build_stack(device, 1, 0, None, None)
+        unsharded = _time_stack(layers1, head1, 1, device, steps, None)
+        del layers1, head1
+        torch.cuda.empty_cache()
+        dist.barrier()
+    coll = tp.Collectives.from_group() if world > 1 else None
+    # decode batches <= 16: row-parallel layers all-reduce through the libebx exchange
+    # (fp32 partials stored into every rank's region over NVLink); larger M: NCCL
+    exchange = (tp.Exchange.from_group(16, 4096)
+                if world > 1 and not getattr(args, "nccl_only", False) else None)
+    layers, head, bits_of = build_stack(device, world, rank, coll, exchange)
+    out = {"workload": "config5: 32 x (QKV 4096->6144 col, O 4096->4096 row, gate/up 4096->14336 "
+                       "col, down 14336->4096 row) + lm_head 4096->128256 col, threshold 0.01; "
+                       f"Megatron TP over {world} GPU(s); row-parallel all-reduce: "
+                       + ("libebx exchange (M<=16), NCCL fp32 (M>16)" if exchange else
+                          "NCCL fp32" if world > 1 else "none") +
+                       "; gate/up interleaved per rank with SwiGLU fused into the decode epilogue (M<=16); "
+                       "integer-code semantics pinned on every rank; greedy ids by a distributed argmax "
+                       "over the lm_head shards; one CUDA graph per decode step",
+           "bits": bits_of}
+    out["parity"] = tp_parity(layers, head, bits_of, world, rank, device, coll)
+    if world > 1:
+        dist.barrier()
+    out.update(_time_stack(layers, head, world, device, steps, coll))
+    if unsharded is not None:
+        out["unsharded"] = unsharded
+        out["efficiency"] = {M: round(out["decode_tok_s"][M] / (world * unsharded["decode_tok_s"][M]), 3)
+                             for M in out["decode_tok_s"]}
+        out["efficiency"]["prefill2048"] = round(
+            out["prefill2048_tok_s"] / (world * unsharded["prefill2048_tok_s"]), 3)
     del layers, head
     if exchange is not None:
         torch.cuda.synchronize()
@@ -788,10 +1025,16 @@ def run_bolt_decoder(device) -> dict:
 # ---------------------------------------------------------------------------
 # CPU: the reference's `pytorch` route restated on the host cores
 # ---------------------------------------------------------------------------
-def cpu_baseline(seconds: float = 8.0, shape=(4096, 4096), bits: int = 10) -> dict:
-    """F.linear(x32, W32) on the host with all threads over the exactly
-    dequantised weight (prepared once, untimed), M in {1, 16}; GB/s of the same
-    algorithmic bytes.  Sample: 4096x4096 at 10 bits, repeated for ~`seconds`."""
+CPU_SHAPES = [(4096, 4096, 10), (4096, 14336, 10), (14336, 4096, 11)]  # (K, N, b at threshold 0.01)
+
+
+def cpu_baseline(seconds: float = 8.0) -> dict:
+    """The reference's `pytorch` route restated on the host (its forward has no CPU
+    path): F.linear(x32, W32) with all host threads over the exactly dequantised
+    weights (prepared once, untimed), over the decode sweep's mix -- the three
+    BASELINE shapes at their threshold-0.01 widths, M in {1, 2, 4, 8, 16} --
+    visited round-robin so the 537 MB of fp32 weights stream from host memory
+    rather than a last-level cache.  GB/s of the same algorithmic bytes."""
     import numpy as np
     import torch
 
@@ -799,33 +1042,36 @@ def cpu_baseline(seconds: float = 8.0, shape=(4096, 4096), bits: int = 10) -> di
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    K, N = shape
-    w = O.baseline_weights(N, K, seed=0)
-    s = O.row_scales(w, bits)
-    q = O.quantize(w, s, bits)
-    W = torch.from_numpy(O.dequantize_codes(q, s).astype(np.float32))
-    total_bytes = 0
-    t_total = 0.0
-    results = {}
-    for M in (1, 16):
-        x = torch.from_numpy(O.normal((M, K), seed=M).astype(np.float16).astype(np.float32))
-        torch.nn.functional.linear(x, W)
-        n = 0
-        t0 = time.perf_counter()
-        while True:
-            torch.nn.functional.linear(x, W)
-            n += 1
-            el = time.perf_counter() - t0
-            if el > seconds / 2:
-                break
-        b = algorithmic_bytes(N, K, bits, M) * n
-        results[str(M)] = round(b / el / 1e9, 3)
-        total_bytes += b
-        t_total += el
-    return {"value": round(total_bytes / t_total / 1e9, 3), "unit": "GB/s", "cores": threads,
+    Ws = []
+    for i, (K, N, bits) in enumerate(CPU_SHAPES):
+        w = O.baseline_weights(N, K, seed=i)
+        sc = O.row_scales(w, bits)
+        q = O.quantize(w, sc, bits)
+        Ws.append((K, N, bits, torch.from_numpy(O.dequantize_codes(q, sc).astype(np.float32))))
+        del w, q
+    xs = {(M, K): torch.from_numpy(O.normal((M, K), seed=M).astype(np.float16).astype(np.float32))
+          for M in MS for K in (4096, 14336)}
+    for K, N, bits, W in Ws:  # touch every weight once before timing
+        torch.nn.functional.linear(xs[(1, K)], W)
+    per_m_bytes = {M: 0 for M in MS}
+    per_m_time = {M: 0.0 for M in MS}
+    t_start = time.perf_counter()
+    rounds = 0
+    while time.perf_counter() - t_start < seconds or rounds == 0:
+        for M in MS:
+            for K, N, bits, W in Ws:
+                t0 = time.perf_counter()
+                torch.nn.functional.linear(xs[(M, K)], W)
+                per_m_time[M] += time.perf_counter() - t0
+                per_m_bytes[M] += algorithmic_bytes(N, K, bits, M)
+        rounds += 1
+    tot_b, tot_t = sum(per_m_bytes.values()), sum(per_m_time.values())
+    per_m = {str(M): round(per_m_bytes[M] / per_m_time[M] / 1e9, 3) for M in MS}
+    return {"value": round(tot_b / tot_t / 1e9, 3), "unit": "GB/s", "cores": threads,
             "kind": "port",
-            "sample": f"F.linear fp32 on host, {N}x{K} dequantised {bits}-bit weight, M in {{1,16}}, "
-                      f"{t_total:.1f}s; per-M GB/s {results}"}
+            "sample": f"F.linear fp32 on the host over the dequantised weights of the 3 BASELINE "
+                      f"shapes (b = 10, 10, 11; 537 MB fp32, round-robin), M in {{1,2,4,8,16}}, "
+                      f"{rounds} rounds in {tot_t:.1f}s; per-M GB/s {per_m}"}
 
 
 def run_reference(args) -> None:
@@ -841,7 +1087,8 @@ def run_reference(args) -> None:
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (host)",
         "data": "synthetic (BASELINE weight scheme, seeded)",
-        "config": {"workload": "config2 decode GEMV sweep sample (4096x4096, M in {1,16})",
+        "config": {"workload": "config2 decode GEMV sweep mix (3 BASELINE shapes at the threshold-0.01 "
+                               "widths, M in {1,2,4,8,16}), bounded host sample",
                    "route": "reference pytorch route restated on host cores (no CPU path exists "
                             "in the reference; its forward is CUDA-only)"},
         "cpu_baseline": cb,
@@ -959,6 +1206,8 @@ def main() -> None:
     ap.add_argument("--impl", default="ebx", choices=["ebx", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip the reference's own CUDA path on the same sweep")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-tp-stack", action="store_true")
     ap.add_argument("--no-bolt", action="store_true", help="skip the config-4 decoder")

@@ -516,6 +516,16 @@ class RuntimeMatrix:
         mlb4.write(path, mlb4.MLB4(self._rows, self._cols, self._bits, self._export_scales(),
                                    self._export_payload(), self._threshold, self._error))
 
+    def _pin_width(self, width: int, planner: str = "pinned") -> None:
+        """Execute at `width` (legal for the storage width) without timing the
+        candidates: tensor-parallel shards pin one width so that every rank runs
+        the same arithmetic whatever its own timing would pick."""
+        if int(width) not in _legal_widths(self._bits):
+            raise ValueError(f"execution width {width} cannot represent {self._bits}-bit codes")
+        self._policy = "fullPrecision" if int(width) == 16 else "hardwareNative"
+        self._set_width(int(width))
+        self._planner = planner
+
     def setDecodePolicy(self, value: str) -> None:
         policy = _parse_policy(value)
         if policy == self._policy:

@@ -215,34 +215,50 @@ class ShardedLinear(torch.nn.Module):
         return part.to(torch.float16)
 
 
+def integer_width(bits: int) -> int:
+    """Integer-code execution width for `bits`-bit codes (4, 8 or 12; 16 when the
+    codes do not fit an exact fp16 operand)."""
+    return 4 if bits <= 4 else 8 if bits <= 8 else 12 if bits <= 12 else 16
+
+
+def _make_matrix(codes, scales, bits: int, threshold: float, error: float, decodePolicy: str,
+                 integer: bool):
+    """A shard's RuntimeMatrix.  integer=True pins the integer-code width (scale
+    after accumulation) on every rank instead of letting each rank's own timing
+    choose, so all ranks execute the same arithmetic."""
+    from .core import RuntimeMatrix
+
+    m = RuntimeMatrix._compressSelectedCodes(codes, scales, bits, threshold, error,
+                                             decodePolicy="fullPrecision" if integer else decodePolicy)
+    if integer:
+        getattr(m, "_native", m)._pin_width(integer_width(bits), planner="tensorParallel")
+    return m
+
+
 def build_sharded(codes, scales, bits: int, mode: str, world: int, rank: int, *,
                   threshold: float = 0.0, error: float = 0.0, bias=None,
                   collectives: Collectives | None = None, gather: bool = False,
                   input_is_local: bool = False, exchange: Exchange | None = None,
-                  decodePolicy: str = "fullPrecision") -> ShardedLinear:
+                  decodePolicy: str = "fullPrecision", integer: bool = False) -> ShardedLinear:
     """Create this rank's shard (libebx matrix) from the global analyzer result."""
-    from .core import RuntimeMatrix
-
     N, K = int(codes.shape[0]), int(codes.shape[1])
     c, s, bounds = shard_codes(codes, scales, mode, world, rank)
     if torch.is_tensor(c):
         c = c.contiguous()
     else:
         c = np.ascontiguousarray(c)
-    m = RuntimeMatrix._compressSelectedCodes(c, s, bits, threshold, error,
-                                             decodePolicy=decodePolicy)
+    m = _make_matrix(c, s, bits, threshold, error, decodePolicy, integer)
     return ShardedLinear(m, mode, N, K, bounds, bias=bias, collectives=collectives, gather=gather,
                          input_is_local=input_is_local, exchange=exchange if mode == "row" else None)
 
 
 def build_column_fused(parts, bits: int, world: int, rank: int, *, threshold: float = 0.0,
-                       error: float = 0.0, decodePolicy: str = "fullPrecision") -> ShardedLinear:
+                       error: float = 0.0, decodePolicy: str = "fullPrecision",
+                       integer: bool = False) -> ShardedLinear:
     """One column-parallel shard holding this rank's rows of several matrices that
     read the same input and share a storage width (gate and up; Q, K and V): the
     rank's slice of each part, concatenated along rows, so one decode launch serves
     them all.  The local output is [part 0 slice | part 1 slice | ...]."""
-    from .core import RuntimeMatrix
-
     cs, ss, widths = [], [], []
     K = int(parts[0][0].shape[1])
     for codes, scales in parts:
@@ -258,7 +274,7 @@ def build_column_fused(parts, bits: int, world: int, rank: int, *, threshold: fl
     else:
         c = np.ascontiguousarray(np.concatenate(cs, 0))
         s = np.ascontiguousarray(np.concatenate(ss, 0))
-    m = RuntimeMatrix._compressSelectedCodes(c, s, bits, threshold, error, decodePolicy=decodePolicy)
+    m = _make_matrix(c, s, bits, threshold, error, decodePolicy, integer)
     lin = ShardedLinear(m, "column", int(c.shape[0]), K, (0, int(c.shape[0])))
     lin.part_widths = widths
     return lin
@@ -285,7 +301,7 @@ class SwiGLULinear(torch.nn.Module):
     forward(x) = silu(x @ Wg_r^T) * (x @ Wu_r^T) over this rank's slice of the
     intermediate dimension.  Decode batches (<= 16 rows) run ebx_linear_swiglu (one
     launch, activation from the fp32 sums); larger batches run ebx_linear on the
-    interleaved matrix and the activation in torch."""
+    interleaved matrix (fp32 sums) and the activation in torch (fp32, one rounding)."""
 
     def __init__(self, matrix, width: int, in_features: int) -> None:
         super().__init__()
@@ -297,17 +313,17 @@ class SwiGLULinear(torch.nn.Module):
         native = getattr(self.matrix, "_native", self.matrix)
         if x.numel() // x.shape[-1] <= 16:
             return native.linear_swiglu(x)
-        y = native.linear(x).view(*x.shape[:-1], self.width // 8, 2, 8)
-        return (torch.nn.functional.silu(y[..., 0, :]) * y[..., 1, :]).reshape(*x.shape[:-1],
-                                                                               self.width)
+        # the fp32 sums, activation in fp32, one rounding (the fused kernel's arithmetic)
+        y = native.linear(x, None, out32=True)[1].view(*x.shape[:-1], self.width // 8, 2, 8)
+        return (torch.nn.functional.silu(y[..., 0, :]) * y[..., 1, :]).reshape(
+            *x.shape[:-1], self.width).to(torch.float16)
 
 
 def build_column_swiglu(gate, up, bits: int, world: int, rank: int, *, threshold: float = 0.0,
-                        error: float = 0.0, decodePolicy: str = "fullPrecision") -> SwiGLULinear:
+                        error: float = 0.0, decodePolicy: str = "fullPrecision",
+                        integer: bool = False) -> SwiGLULinear:
     """This rank's column slice of a gate/up pair (global codes and scales each, same
     width) as one interleaved matrix with the SwiGLU activation fused."""
-    from .core import RuntimeMatrix
-
     (gc, gs), (uc, us) = gate, up
     K = int(gc.shape[1])
     cg, sg, (lo, hi) = shard_codes(gc, gs, "column", world, rank)
@@ -316,10 +332,28 @@ def build_column_swiglu(gate, up, bits: int, world: int, rank: int, *, threshold
     c = interleave_by8(cg, cu)
     s = interleave_by8(sg if torch.is_tensor(sg) else np.asarray(sg),
                        su if torch.is_tensor(su) else np.asarray(su))
-    m = RuntimeMatrix._compressSelectedCodes(c, s, bits, threshold, error, decodePolicy=decodePolicy)
+    m = _make_matrix(c, s, bits, threshold, error, decodePolicy, integer)
     return SwiGLULinear(m, width, K)
+
+
+def greedy_argmax(local_logits: torch.Tensor, offset: int,
+                  collectives: Collectives | None) -> torch.Tensor:
+    """Greedy next-token ids from column-parallel logits: each rank reduces its
+    vocabulary slice [offset, offset + width) to (max value, global index) per
+    row, one all-gather exchanges those pairs, and every rank picks the largest
+    value, the lowest index among equal values (torch.argmax's rule on the full
+    logits; shards are in rank order, so the first maximum wins).  The indices
+    travel as fp32, exact below 2^24 (the 128256-entry vocabulary fits)."""
+    val, idx = local_logits.float().max(dim=-1)
+    pair = torch.stack([val, (idx + int(offset)).float()], dim=-1)  # [M, 2]
+    if collectives is None:
+        return pair[..., 1].long()
+    allp = collectives.allgather(pair)                                # [M, 2 * world]
+    vals, ids = allp[..., 0::2], allp[..., 1::2]
+    best = vals.argmax(dim=-1, keepdim=True)
+    return ids.gather(-1, best).squeeze(-1).long()
 
 
 __all__ = ["MODES", "shard_bounds", "shard_codes", "Collectives", "Exchange", "ShardedLinear",
            "build_sharded", "build_column_fused", "interleave_by8", "SwiGLULinear",
-           "build_column_swiglu"]
+           "build_column_swiglu", "greedy_argmax", "integer_width"]

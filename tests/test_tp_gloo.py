@@ -142,3 +142,40 @@ def test_swiglu_module_large_batch_deinterleaves():
     g = x @ torch.from_numpy(wg).T
     u = x @ torch.from_numpy(wu).T
     assert torch.allclose(y, torch.nn.functional.silu(g) * u, atol=1e-5)
+
+
+def _argmax_worker(rank, world, port, result_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        vocab = 1000
+        g = torch.Generator().manual_seed(3)
+        logits = torch.randn((5, vocab), generator=g).half()
+        # ties across a shard boundary and inside one shard: the lowest index must win
+        lo0, hi0 = tp.shard_bounds(vocab, world, 0, 16)
+        logits[1, hi0] = 9.0
+        logits[1, hi0 - 1] = 9.0
+        logits[2, 7] = 9.0
+        logits[2, 3] = 9.0
+        lo, hi = tp.shard_bounds(vocab, world, rank, 16)
+        ids = tp.greedy_argmax(logits[:, lo:hi], lo, tp.Collectives.from_group())
+        result_q.put((rank, ids.tolist(), logits.float().argmax(dim=-1).tolist()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_greedy_argmax_over_column_shards():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_argmax_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for _, ids, ref in res:
+        assert ids == ref
