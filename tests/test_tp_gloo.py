@@ -123,7 +123,8 @@ def test_interleave_by8_layout_numpy_and_torch():
 
 
 def test_swiglu_module_large_batch_deinterleaves():
-    """M > 16 path: ebx_linear on the interleaved matrix, activation in torch."""
+    """M > 16 path: ebx_linear's fp32 sums on the interleaved matrix, activation in
+    torch in fp32, one rounding to fp16."""
     from mlbricks_b200.elasticbit.tensor_parallel import SwiGLULinear, interleave_by8
 
     rng = np.random.default_rng(0)
@@ -133,15 +134,17 @@ def test_swiglu_module_large_batch_deinterleaves():
     w = torch.from_numpy(interleave_by8(wg, wu))
 
     class Stand:
-        def linear(self, x):
-            return x @ w.T
+        def linear(self, x, bias=None, out32=False):
+            y32 = x.float() @ w.T
+            return (y32.half(), y32) if out32 else y32.half()
 
     mod = SwiGLULinear(Stand(), I, K)
     x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32))
     y = mod(x)
+    assert y.dtype == torch.float16
     g = x @ torch.from_numpy(wg).T
     u = x @ torch.from_numpy(wu).T
-    assert torch.allclose(y, torch.nn.functional.silu(g) * u, atol=1e-5)
+    assert torch.equal(y, (torch.nn.functional.silu(g) * u).half())
 
 
 def _argmax_worker(rank, world, port, result_q):
