@@ -21,6 +21,7 @@ codes and scales are the reference's on the same GPU.
 from __future__ import annotations
 
 import gc
+import io
 import json
 import os
 import tempfile
@@ -46,60 +47,74 @@ _CALIBRATION_ROWS = 32  # rows kept per Linear during calibration (core.py:734)
 
 
 def _checkPolicy(value: str) -> str:
-    value = str(value)
+    """The decode policy name, validated (ValueError with the reference's message)."""
     if value not in _POLICIES:
         raise ValueError("decodePolicy must be 'hardwareNative' or 'fullPrecision'")
-    return value
+    return str(value)
 
 
-def _toNumpy2D(value: Any, *, name: str) -> np.ndarray:
+def _as_f32_matrix(value: Any, name: str) -> np.ndarray:
+    """A host float32 C-contiguous 2-D array from a tensor, array or nested list."""
     if torch.is_tensor(value):
-        value = value.detach().float().cpu().numpy()
-    arr = np.asarray(value, dtype=np.float32)
+        arr = value.detach().to(device="cpu", dtype=torch.float32).numpy()
+    else:
+        arr = np.asarray(value, dtype=np.float32)
     if arr.ndim != 2:
         raise ValueError(f"{name} must be a 2D matrix")
-    return np.ascontiguousarray(arr, dtype=np.float32)
+    return np.require(arr, dtype=np.float32, requirements="C")
 
 
-def _toCalibrationBatches(calibrationData: Any) -> list[Any]:
-    if torch.is_tensor(calibrationData) or isinstance(calibrationData, Mapping):
-        return [calibrationData]
-    if isinstance(calibrationData, (str, bytes)):
-        raise TypeError("calibrationData must contain model inputs, not text")
-    try:
-        batches = list(calibrationData)
-    except TypeError as exc:
-        raise TypeError(
-            "calibrationData must be a model input or an iterable of model inputs") from exc
-    if not batches:
-        raise ValueError("calibrationData cannot be empty")
-    return batches
+class _CalibrationFeed:
+    """ElasticBit.compress's calibrationData as a list of model calls.
 
+    One tensor or mapping is one call; any other iterable is a sequence of calls
+    (tuple entries are positional arguments, mappings keyword arguments).
+    """
 
-def _callModel(model: nn.Module, batch: Any) -> Any:
-    if isinstance(batch, Mapping):
-        return model(**batch)
-    if isinstance(batch, tuple):
-        return model(*batch)
-    return model(batch)
+    def __init__(self, data: Any) -> None:
+        if torch.is_tensor(data) or isinstance(data, Mapping):
+            self.batches = [data]
+            return
+        if isinstance(data, (str, bytes)):
+            raise TypeError("calibrationData must contain model inputs, not text")
+        try:
+            self.batches = list(data)
+        except TypeError as exc:
+            raise TypeError(
+                "calibrationData must be a model input or an iterable of model inputs") from exc
+        if not self.batches:
+            raise ValueError("calibrationData cannot be empty")
 
+    @classmethod
+    def _on(cls, obj: Any, device: torch.device) -> Any:
+        if torch.is_tensor(obj):
+            return obj.to(device)
+        if isinstance(obj, Mapping):
+            return {key: cls._on(val, device) for key, val in obj.items()}
+        if isinstance(obj, list):
+            return [cls._on(val, device) for val in obj]
+        if isinstance(obj, tuple):
+            return tuple(cls._on(val, device) for val in obj)
+        return obj
 
-def _moveBatch(batch: Any, device: torch.device) -> Any:
-    if torch.is_tensor(batch):
-        return batch.to(device)
-    if isinstance(batch, Mapping):
-        return {k: _moveBatch(v, device) for k, v in batch.items()}
-    if isinstance(batch, (tuple, list)):
-        moved = [_moveBatch(v, device) for v in batch]
-        return tuple(moved) if isinstance(batch, tuple) else moved
-    return batch
+    def replay(self, model: nn.Module, device: torch.device) -> None:
+        with torch.inference_mode():
+            for batch in self.batches:
+                args = self._on(batch, device)
+                if isinstance(args, Mapping):
+                    model(**args)
+                elif isinstance(args, tuple):
+                    model(*args)
+                else:
+                    model(args)
 
 
 def _relativeL2Torch(reference: torch.Tensor, candidate: torch.Tensor) -> float:
-    ref = reference.float()
-    cand = candidate.float()
-    den = torch.linalg.vector_norm(ref).clamp_min(1.0e-30)
-    return float((torch.linalg.vector_norm(cand - ref) / den).item())
+    """||candidate - reference|| / max(||reference||, 1e-30) in fp32 (the reference
+    analyzer's error measure, same operations so the same bits)."""
+    r, c = reference.float(), candidate.float()
+    return float((torch.linalg.vector_norm(c - r)
+                  / torch.linalg.vector_norm(r).clamp_min(1.0e-30)).item())
 
 
 @torch.inference_mode()
@@ -144,21 +159,20 @@ def _selectBitsTorch(weight: torch.Tensor, calibration: np.ndarray, threshold: f
 
 
 def _moduleDevice(module: nn.Module) -> torch.device:
-    for p in module.parameters():
-        return p.device
-    for b in module.buffers():
-        return b.device
-    return torch.device("cpu")
+    """Device of the module's first parameter (else first buffer, else CPU)."""
+    first = next(module.parameters(), None)
+    if first is None:
+        first = next(module.buffers(), None)
+    return first.device if first is not None else torch.device("cpu")
 
 
-def _replaceNamedModule(root: nn.Module, name: str, replacement: nn.Module) -> None:
-    if not name:
+def _swap_module(root: nn.Module, name: str, replacement: nn.Module) -> None:
+    """Put `replacement` at dotted path `name` inside `root`."""
+    parent_name, _, leaf = name.rpartition(".")
+    if not leaf:
         raise ValueError("ElasticBit cannot replace the root module")
-    *parents, leaf = name.split(".")
-    owner = root
-    for part in parents:
-        owner = owner._modules[part]
-    owner._modules[leaf] = replacement
+    parent = root.get_submodule(parent_name) if parent_name else root
+    parent._modules[leaf] = replacement
 
 
 @dataclass(frozen=True)
@@ -222,8 +236,8 @@ class RuntimeMatrix:
                  decodePolicy: str = "hardwareNative") -> "RuntimeMatrix":
         native = _requireNative()
         policy = _checkPolicy(decodePolicy)
-        w = _toNumpy2D(weights, name="weights")
-        c = _toNumpy2D(calibrationData, name="calibrationData")
+        w = _as_f32_matrix(weights, "weights")
+        c = _as_f32_matrix(calibrationData, "calibrationData")
         return cls(native.RuntimeMatrix.compress(w, c, float(threshold), policy))
 
     @classmethod
@@ -232,7 +246,7 @@ class RuntimeMatrix:
                           decodePolicy: str = "hardwareNative") -> "RuntimeMatrix":
         native = _requireNative()
         policy = _checkPolicy(decodePolicy)
-        w = _toNumpy2D(weights, name="weights")
+        w = _as_f32_matrix(weights, "weights")
         return cls(native.RuntimeMatrix._compressSelected(
             w, int(selectedBits), float(threshold), float(selectedError), policy))
 
@@ -387,6 +401,13 @@ class _ElasticLinear(nn.Module):
 
 
 class _ModelElasticBit:
+    """Controller attached as ``model.elasticbit`` by ElasticBit.compress / load.
+
+    Holds the artifact-level facts (threshold, policy, which Linears were
+    compressed or left alone) and applies policy / backend changes to every
+    compressed layer; matrices shared by several layers are switched once.
+    """
+
     def __init__(self, model: nn.Module, threshold: float, decodePolicy: str,
                  compressedNames: Sequence[str], skippedNames: Sequence[str],
                  optimizationProfiles: Mapping[str, Any] | None = None) -> None:
@@ -398,55 +419,67 @@ class _ModelElasticBit:
         self.optimizationProfiles = dict(optimizationProfiles or {})
         self.activeOptimization: dict[str, Any] | None = None
 
-    def _layers(self) -> list[tuple[str, _ElasticLinear]]:
-        modules = dict(self._model.named_modules())
-        return [(n, modules[n]) for n in self.compressedNames
-                if isinstance(modules.get(n), _ElasticLinear)]
+    def _compressed_layers(self) -> Iterable[tuple[str, "_ElasticLinear"]]:
+        for name in self.compressedNames:
+            try:
+                layer = self._model.get_submodule(name)
+            except AttributeError:
+                continue
+            if isinstance(layer, _ElasticLinear):
+                yield name, layer
+
+    def _matrices(self) -> Iterable[RuntimeMatrix]:
+        seen: set[int] = set()
+        for _, layer in self._compressed_layers():
+            if id(layer.matrix) not in seen:
+                seen.add(id(layer.matrix))
+                yield layer.matrix
 
     def setDecodePolicy(self, decodePolicy: str) -> "_ModelElasticBit":
         policy = _checkPolicy(decodePolicy)
-        done: set[int] = set()
-        for _, layer in self._layers():
-            if id(layer.matrix) not in done:
-                layer.matrix.setDecodePolicy(policy)
-                done.add(id(layer.matrix))
+        for matrix in self._matrices():
+            matrix.setDecodePolicy(policy)
         self.decodePolicy = policy
         return self
 
     def setBackend(self, backend: str) -> "_ModelElasticBit":
-        for _, layer in self._layers():
+        for _, layer in self._compressed_layers():
             layer.set_backend(backend)
         return self
 
     def summary(self) -> str:
-        be = ElasticBit.backend()
-        lines = [
-            "ElasticBit Summary",
-            "-" * 60,
-            f"Threshold       : {self.threshold}",
-            f"Decode Policy   : {self.decodePolicy}",
-            f"Backend         : {be.architecture or 'unavailable'}",
-            f"Prefill         : {be.prefill or 'unknown'}",
-            f"Decode Engine   : {be.decodeEngine or 'unknown'}",
-            f"Decode Status   : {be.decodeStatus or 'unknown'}",
-            f"Decode Planner  : {be.decodePlanner or 'unknown'}",
-            f"Decode Validate : {be.decodeValidation or 'unknown'}",
-            f"Activate DType  : {be.activateDType or 'unknown'}",
-            f"Optimize Cache  : {len(self.optimizationProfiles)} profile(s)",
-            "Optimize Active : " + ("none" if self.activeOptimization is None
-                                    else str(self.activeOptimization.get("planner", "unknown"))),
-            "",
-            f"{'Layer':36s} {'Stored':>8s} {'Execute':>10s} {'Planner':>14s} {'Error':>10s}",
+        """Print and return a per-layer table: stored width, execution width,
+        planner and selected error, after the backend facts."""
+        info = ElasticBit.backend()
+        active = self.activeOptimization
+        facts = [
+            ("Threshold", self.threshold),
+            ("Decode Policy", self.decodePolicy),
+            ("Backend", info.architecture or "unavailable"),
+            ("Prefill", info.prefill or "unknown"),
+            ("Decode Engine", info.decodeEngine or "unknown"),
+            ("Decode Status", info.decodeStatus or "unknown"),
+            ("Decode Planner", info.decodePlanner or "unknown"),
+            ("Decode Validate", info.decodeValidation or "unknown"),
+            ("Activate DType", info.activateDType or "unknown"),
+            ("Optimize Cache", f"{len(self.optimizationProfiles)} profile(s)"),
+            ("Optimize Active", "none" if active is None else str(active.get("planner", "unknown"))),
         ]
-        for name, layer in self._layers():
+        widths = (36, 8, 10, 14, 10)
+        cells = [("Layer", "Stored", "Execute", "Planner", "Error")]
+        for name, layer in self._compressed_layers():
             m = layer.matrix
-            lines.append(f"{name[:36]:36s} {str(m.storageBits) + '-bit':>8s} "
-                         f"{'W' + str(m.executionWidth) + 'A16':>10s} "
-                         f"{m.executionPlanner:>14s} {m.error:10.6f}")
+            cells.append((name[:36], f"{m.storageBits}-bit", f"W{m.executionWidth}A16",
+                          m.executionPlanner, f"{m.error:.6f}"))
+        out = ["ElasticBit Summary", "-" * 60]
+        out += [f"{label:<16s}: {value}" for label, value in facts]
+        out.append("")
+        out += [" ".join([row[0].ljust(widths[0])] + [c.rjust(w) for c, w in zip(row[1:], widths[1:])])
+                for row in cells]
         if self.skippedNames:
-            lines += ["", "Uncompressed (no safe calibration path):"]
-            lines += [f"  {n}" for n in self.skippedNames]
-        text = "\n".join(lines)
+            out += ["", "Uncompressed (no safe calibration path):"]
+            out += ["  " + n for n in self.skippedNames]
+        text = "\n".join(out)
         print(text)
         return text
 
@@ -467,6 +500,177 @@ def _semanticOutputWeightIds(model: nn.Module) -> set[int]:
     return {id(head.weight)} if isinstance(head, nn.Linear) else set()
 
 
+class _RowRecorder:
+    """Forward pre-hooks that keep, per Linear name, the first `limit` input rows
+    the Linear sees during the calibration pass (the reference analyzes only the
+    first 32 rows of each Linear, core.py:734)."""
+
+    def __init__(self, limit: int) -> None:
+        self.limit = int(limit)
+        self._rows: dict[str, list[torch.Tensor]] = {}
+        self._count: dict[str, int] = {}
+
+    def _pre_hook(self, name: str):
+        def record(_module: nn.Module, inputs: tuple[Any, ...]) -> None:
+            if not inputs or not torch.is_tensor(inputs[0]):
+                return
+            room = self.limit - self._count.get(name, 0)
+            if room <= 0:
+                return
+            x = inputs[0].detach()
+            kept = x.reshape(-1, x.shape[-1])[:room].float().cpu()
+            self._rows.setdefault(name, []).append(kept)
+            self._count[name] = self._count.get(name, 0) + int(kept.shape[0])
+        return record
+
+    def capture(self, model: nn.Module, names: Sequence[str], feed: _CalibrationFeed,
+                device: torch.device) -> None:
+        handles = [model.get_submodule(n).register_forward_pre_hook(self._pre_hook(n))
+                   for n in names]
+        try:
+            feed.replay(model, device)
+        finally:
+            for h in handles:
+                h.remove()
+
+    def rows_for(self, names: Sequence[str]) -> np.ndarray | None:
+        """The recorded rows of `names` (in that order) as one float32 matrix."""
+        parts = [t for n in names for t in self._rows.get(n, ())]
+        if not parts:
+            return None
+        return np.ascontiguousarray(torch.cat(parts, 0).numpy(), dtype=np.float32)
+
+    def release(self, names: Sequence[str]) -> None:
+        for n in names:
+            self._rows.pop(n, None)
+
+
+@dataclass
+class _LinearGroup:
+    """All Linear modules that share one weight tensor (compressed once)."""
+    names: list[str]
+    output_head: bool  # the preserved semantic output head: kept FP16, listed as skipped
+    tied: bool         # weight shared with an embedding: kept FP16 silently
+
+
+def _linear_groups(model: nn.Module, preserve_head: bool) -> list[_LinearGroup]:
+    embedding = {id(m.weight) for m in model.modules() if isinstance(m, nn.Embedding)}
+    heads = _semanticOutputWeightIds(model) if preserve_head else set()
+    groups: dict[int, _LinearGroup] = {}
+    for name, module in model.named_modules():
+        if isinstance(module, nn.Linear):
+            key = id(module.weight)
+            if key not in groups:
+                groups[key] = _LinearGroup([], key in heads, key in embedding)
+            groups[key].names.append(name)
+    return list(groups.values())
+
+
+def _compress_linear(module: nn.Linear, rows: np.ndarray, threshold: float, policy: str,
+                     device: torch.device) -> tuple[RuntimeMatrix, int, float]:
+    """Width selection on the module's FP16 weight, then the matrix on its GPU."""
+    bits, err, codes, scales = _selectBitsTorch(module.weight, rows, threshold)
+    with torch.cuda.device(device):
+        if bits <= 15:
+            matrix = RuntimeMatrix._compressSelectedCodes(codes, scales, bits, threshold, err,
+                                                          decodePolicy=policy)
+        else:  # 16: the FP16 weight itself
+            matrix = RuntimeMatrix._compressSelected(module.weight.detach().float(), bits,
+                                                     threshold, err, decodePolicy=policy)
+    return matrix, bits, err
+
+
+def _progress_enabled() -> bool:
+    flag = os.environ.get("MLBRICKS_ELASTICBIT_PROGRESS", "")
+    return flag.strip().lower() in {"1", "true", "yes", "on"}
+
+
+def _write_artifact(model: nn.Module, ctl: "_ModelElasticBit", dest: Path) -> None:
+    """The `.elasticbit` zip: manifest.json (the reference writer's keys and order),
+    one MLB4 file per distinct matrix under matrices/, and state.pt (the model's
+    state_dict).  Matrices are staged through a temporary file (the runtime writes
+    MLB4 to a path); the manifest and state go straight into the archive."""
+    layers: list[dict[str, Any]] = []
+    members: dict[int, str] = {}
+    with tempfile.TemporaryDirectory(prefix="elasticbit-save-") as tmp, \
+            zipfile.ZipFile(dest, "w", compression=zipfile.ZIP_DEFLATED) as zf:
+        for name in ctl.compressedNames:
+            try:
+                layer = model.get_submodule(name)
+            except AttributeError:
+                layer = None
+            if not isinstance(layer, _ElasticLinear):
+                raise RuntimeError(f"ElasticBit layer disappeared before save: {name}")
+            member = members.get(id(layer.matrix))
+            if member is None:
+                member = f"matrix_{len(members):05d}.mlb"
+                members[id(layer.matrix)] = member
+                staged = Path(tmp) / member
+                layer.matrix.save(staged)
+                zf.write(staged, f"matrices/{member}")
+            layers.append({"name": name, "matrix": member, "inFeatures": layer.inFeatures,
+                           "outFeatures": layer.outFeatures, "hasBias": layer.bias is not None})
+        manifest = {
+            "format": _ARTIFACT_FORMAT,
+            "version": _ARTIFACT_VERSION,
+            "threshold": ctl.threshold,
+            "decodePolicy": ctl.decodePolicy,
+            "compressedNames": list(ctl.compressedNames),
+            "skippedNames": list(ctl.skippedNames),
+            "optimizationProfiles": ctl.optimizationProfiles,
+            "layers": layers,
+        }
+        zf.writestr("manifest.json", json.dumps(manifest, indent=2))
+        state = io.BytesIO()
+        torch.save(model.state_dict(), state)
+        zf.writestr("state.pt", state.getvalue())
+
+
+def _read_artifact(model: nn.Module, src: Path, policy: str, route: str) -> nn.Module:
+    """Rebuild a `.elasticbit` artifact's compressed layers inside `model` (the
+    architecture), then load its state_dict; each MLB4 member is loaded once and
+    shared by every layer entry naming it."""
+    with zipfile.ZipFile(src, "r") as zf:
+        manifest = json.loads(zf.read("manifest.json").decode("utf-8"))
+        if (manifest.get("format") != _ARTIFACT_FORMAT
+                or manifest.get("version") != _ARTIFACT_VERSION):
+            raise ValueError("Unsupported ElasticBit model artifact")
+        matrices: dict[str, RuntimeMatrix] = {}
+        names: list[str] = []
+        with tempfile.TemporaryDirectory(prefix="elasticbit-load-") as tmp:
+            for entry in manifest["layers"]:
+                name = str(entry["name"])
+                try:
+                    target = model.get_submodule(name)
+                except AttributeError:
+                    target = None
+                if not isinstance(target, nn.Linear):
+                    raise ValueError(
+                        f"Model architecture does not contain expected Linear layer: {name}")
+                device = target.weight.device
+                if device.type != "cuda":
+                    raise RuntimeError("ElasticBit.load() requires the target model on CUDA")
+                member = str(entry["matrix"])
+                if member not in matrices:
+                    staged = Path(tmp) / Path(member).name
+                    staged.write_bytes(zf.read(f"matrices/{member}"))
+                    with torch.cuda.device(device):
+                        matrices[member] = RuntimeMatrix.load(staged, decodePolicy=policy)
+                bias = target.bias if bool(entry["hasBias"]) else None
+                layer = _ElasticLinear(matrices[member], int(entry["inFeatures"]),
+                                       int(entry["outFeatures"]), bias, backend=route)
+                _swap_module(model, name, layer.to(device=device))
+                names.append(name)
+        state = torch.load(io.BytesIO(zf.read("state.pt")), map_location=_moduleDevice(model),
+                           weights_only=True)
+    model.load_state_dict(state, strict=True)
+    model.elasticbit = _ModelElasticBit(
+        model, threshold=float(manifest["threshold"]), decodePolicy=policy,
+        compressedNames=names, skippedNames=tuple(manifest.get("skippedNames", ())),
+        optimizationProfiles=manifest.get("optimizationProfiles", {}))
+    return model
+
+
 class ElasticBit:
     """ElasticBit public namespace."""
 
@@ -475,8 +679,8 @@ class ElasticBit:
     @staticmethod
     def analyze(weights: Any, calibrationData: Any, threshold: float) -> BitAnalysis:
         native = _requireNative()
-        raw = native.analyze(_toNumpy2D(weights, name="weights"),
-                             _toNumpy2D(calibrationData, name="calibrationData"),
+        raw = native.analyze(_as_f32_matrix(weights, "weights"),
+                             _as_f32_matrix(calibrationData, "calibrationData"),
                              float(threshold))
         cands = tuple(BitCandidate(
             bits=int(c["bits"]), hardwareNativeError=float(c["hardwareNativeError"]),
@@ -549,150 +753,83 @@ class ElasticBit:
     def compress(model: nn.Module, calibrationData: Any, threshold: float,
                  decodePolicy: str = "hardwareNative", preserveOutputHead: bool = True,
                  backend: str = "auto") -> nn.Module:
+        """Replace every compressible nn.Linear of a CUDA FP16 model by an ElasticBit
+        layer whose storage width the calibration pass selects (reference:
+        core.py:695-898; `backend` is an additive keyword choosing the route)."""
         if not isinstance(model, nn.Module):
             raise TypeError("ElasticBit.compress() expects a torch.nn.Module")
         _requireNative()
         policy = _checkPolicy(decodePolicy)
         route = normalize_backend(backend)
-        batches = _toCalibrationBatches(calibrationData)
+        feed = _CalibrationFeed(calibrationData)
         device = _moduleDevice(model)
         if device.type != "cuda":
             raise RuntimeError("ElasticBit model compression currently requires a CUDA model")
-        for module in model.modules():
-            if isinstance(module, nn.Linear) and module.weight.dtype != torch.float16:
-                raise RuntimeError(
-                    "ElasticBit.compress() currently requires FP16 Linear weights. "
-                    "Convert the model to float16 before compression.")
+        if any(isinstance(m, nn.Linear) and m.weight.dtype != torch.float16
+               for m in model.modules()):
+            raise RuntimeError(
+                "ElasticBit.compress() currently requires FP16 Linear weights. "
+                "Convert the model to float16 before compression.")
 
-        embedding_ids = {id(m.weight) for m in model.modules() if isinstance(m, nn.Embedding)}
-        head_ids = _semanticOutputWeightIds(model) if bool(preserveOutputHead) else set()
-        protected = embedding_ids | head_ids
-
-        # Calibration capture: the first 32 input rows each Linear sees.
-        captured: dict[str, list[np.ndarray]] = {}
-
-        def make_hook(name: str):
-            def hook(_mod: nn.Module, inputs: tuple[Any, ...]) -> None:
-                if not inputs or not torch.is_tensor(inputs[0]):
-                    return
-                t = inputs[0]
-                have = sum(a.shape[0] for a in captured.get(name, []))
-                room = _CALIBRATION_ROWS - have
-                if room <= 0:
-                    return
-                rows = t.detach().float().reshape(-1, t.shape[-1])[:room]
-                captured.setdefault(name, []).append(rows.cpu().numpy().astype(np.float32))
-            return hook
-
-        names_by_weight: dict[int, list[str]] = {}
-        hooks = []
-        for name, module in model.named_modules():
-            if isinstance(module, nn.Linear):
-                names_by_weight.setdefault(id(module.weight), []).append(name)
-                if id(module.weight) not in protected:
-                    hooks.append(module.register_forward_pre_hook(make_hook(name)))
+        groups = _linear_groups(model, bool(preserveOutputHead))
+        work = [g for g in groups if not (g.output_head or g.tied)]
+        recorder = _RowRecorder(_CALIBRATION_ROWS)
         model.eval()
-        try:
-            with torch.inference_mode():
-                for batch in batches:
-                    _callModel(model, _moveBatch(batch, device))
-        finally:
-            for h in hooks:
-                h.remove()
+        recorder.capture(model, [n for g in work for n in g.names], feed, device)
 
-        skipped = [n for wid, names in names_by_weight.items() if wid in head_ids for n in names]
+        skipped = [n for g in groups if g.output_head for n in g.names]
         compressed: list[str] = []
-        todo = [(wid, names) for wid, names in names_by_weight.items() if wid not in protected]
-        progress = os.environ.get("MLBRICKS_ELASTICBIT_PROGRESS", "").strip().lower() in {
-            "1", "true", "yes", "on"}
-
-        for index, (_, names) in enumerate(todo, start=1):
-            module = model.get_submodule(names[0])
-            if not isinstance(module, nn.Linear):
-                raise RuntimeError(f"ElasticBit expected Linear module at {names[0]}")
-            parts = [a for n in names for a in captured.get(n, [])]
-            if not parts:
-                skipped.extend(names)
+        verbose = _progress_enabled()
+        thr = float(threshold)
+        for index, group in enumerate(work, start=1):
+            rows = recorder.rows_for(group.names)
+            if rows is None:  # never reached by the calibration inputs
+                skipped.extend(group.names)
                 continue
-            calib = np.ascontiguousarray(np.concatenate(parts, axis=0), dtype=np.float32)
-            if progress:
-                print(f"[ElasticBit] {index}/{len(todo)} analyzing {names[0]} "
-                      f"shape={tuple(module.weight.shape)} rows={calib.shape[0]}", flush=True)
-            bits, err, codes, scales = _selectBitsTorch(module.weight, calib, float(threshold))
-            with torch.cuda.device(device):
-                if bits <= 15:
-                    matrix = RuntimeMatrix._compressSelectedCodes(
-                        codes, scales, bits, float(threshold), err, decodePolicy=policy)
-                else:
-                    matrix = RuntimeMatrix._compressSelected(
-                        module.weight.detach().float(), bits, float(threshold), err,
-                        decodePolicy=policy)
-            if progress:
-                print(f"[ElasticBit] {index}/{len(todo)} selected {bits}-bit error={err:.6g}",
+            module = model.get_submodule(group.names[0])
+            if not isinstance(module, nn.Linear):
+                raise RuntimeError(f"ElasticBit expected Linear module at {group.names[0]}")
+            if verbose:
+                print(f"[ElasticBit] {index}/{len(work)} analyzing {group.names[0]} "
+                      f"shape={tuple(module.weight.shape)} rows={rows.shape[0]}", flush=True)
+            matrix, bits, err = _compress_linear(module, rows, thr, policy, device)
+            if verbose:
+                print(f"[ElasticBit] {index}/{len(work)} selected {bits}-bit error={err:.6g}",
                       flush=True)
-            for name in names:
+            for name in group.names:
                 current = model.get_submodule(name)
                 if not isinstance(current, nn.Linear):
                     raise RuntimeError(f"ElasticBit expected Linear module at {name}")
-                repl = _ElasticLinear(matrix, current.in_features, current.out_features,
-                                      current.bias, backend=route).to(device=device)
-                _replaceNamedModule(model, name, repl)
+                layer = _ElasticLinear(matrix, current.in_features, current.out_features,
+                                       current.bias, backend=route)
+                _swap_module(model, name, layer.to(device=device))
                 compressed.append(name)
-                captured.pop(name, None)
-            del module, codes, scales, calib, parts, matrix
+            recorder.release(group.names)
+            del module, matrix, rows
             gc.collect()
             torch.cuda.empty_cache()
 
-        model.elasticbit = _ModelElasticBit(model, threshold=float(threshold), decodePolicy=policy,
+        model.elasticbit = _ModelElasticBit(model, threshold=thr, decodePolicy=policy,
                                             compressedNames=compressed, skippedNames=skipped)
         return model
 
     @staticmethod
     def save(model: nn.Module, path: str | Path) -> Path:
+        """Write the compressed model as a `.elasticbit` artifact (reference:
+        core.py:900-953; same members, manifest keys and MLB4 files)."""
         ctl = getattr(model, "elasticbit", None)
         if not isinstance(ctl, _ModelElasticBit):
             raise ValueError("ElasticBit.save() expects a model produced by ElasticBit.compress()")
         dest = Path(path)
         dest.parent.mkdir(parents=True, exist_ok=True)
-        modules = dict(model.named_modules())
-        with tempfile.TemporaryDirectory(prefix="elasticbit-save-") as tmp:
-            root = Path(tmp)
-            (root / "matrices").mkdir()
-            files: dict[int, str] = {}
-            layers = []
-            for name in ctl.compressedNames:
-                layer = modules.get(name)
-                if not isinstance(layer, _ElasticLinear):
-                    raise RuntimeError(f"ElasticBit layer disappeared before save: {name}")
-                fname = files.get(id(layer.matrix))
-                if fname is None:
-                    fname = f"matrix_{len(files):05d}.mlb"
-                    layer.matrix.save(root / "matrices" / fname)
-                    files[id(layer.matrix)] = fname
-                layers.append({"name": name, "matrix": fname, "inFeatures": layer.inFeatures,
-                               "outFeatures": layer.outFeatures,
-                               "hasBias": layer.bias is not None})
-            manifest = {
-                "format": _ARTIFACT_FORMAT,
-                "version": _ARTIFACT_VERSION,
-                "threshold": ctl.threshold,
-                "decodePolicy": ctl.decodePolicy,
-                "compressedNames": list(ctl.compressedNames),
-                "skippedNames": list(ctl.skippedNames),
-                "optimizationProfiles": ctl.optimizationProfiles,
-                "layers": layers,
-            }
-            (root / "manifest.json").write_text(json.dumps(manifest, indent=2), encoding="utf-8")
-            torch.save(model.state_dict(), root / "state.pt")
-            with zipfile.ZipFile(dest, "w", compression=zipfile.ZIP_DEFLATED) as zf:
-                for f in sorted(root.rglob("*")):
-                    if f.is_file():
-                        zf.write(f, f.relative_to(root).as_posix())
+        _write_artifact(model, ctl, dest)
         return dest
 
     @staticmethod
     def load(model: nn.Module, path: str | Path, decodePolicy: str = "hardwareNative",
              backend: str = "auto") -> nn.Module:
+        """Restore a `.elasticbit` artifact into `model`, the uncompressed architecture
+        (reference: core.py:955-1017)."""
         if not isinstance(model, nn.Module):
             raise TypeError("ElasticBit.load() requires the model architecture as its first argument")
         _requireNative()
@@ -700,47 +837,5 @@ class ElasticBit:
         if not src.exists():
             raise FileNotFoundError(src)
         route = normalize_backend(backend)
-        with tempfile.TemporaryDirectory(prefix="elasticbit-load-") as tmp:
-            root = Path(tmp)
-            with zipfile.ZipFile(src, "r") as zf:
-                zf.extractall(root)
-            manifest = json.loads((root / "manifest.json").read_text(encoding="utf-8"))
-            if (manifest.get("format") != _ARTIFACT_FORMAT
-                    or manifest.get("version") != _ARTIFACT_VERSION):
-                raise ValueError("Unsupported ElasticBit model artifact")
-            policy = _checkPolicy(decodePolicy)
-            modules = dict(model.named_modules())
-            cache: dict[str, RuntimeMatrix] = {}
-            names: list[str] = []
-            for entry in manifest["layers"]:
-                name = str(entry["name"])
-                target = modules.get(name)
-                if not isinstance(target, nn.Linear):
-                    raise ValueError(
-                        f"Model architecture does not contain expected Linear layer: {name}")
-                device = target.weight.device
-                if device.type != "cuda":
-                    raise RuntimeError("ElasticBit.load() requires the target model on CUDA")
-                fname = str(entry["matrix"])
-                matrix = cache.get(fname)
-                if matrix is None:
-                    with torch.cuda.device(device):
-                        matrix = RuntimeMatrix.load(root / "matrices" / fname, decodePolicy=policy)
-                    cache[fname] = matrix
-                repl = _ElasticLinear(matrix, int(entry["inFeatures"]), int(entry["outFeatures"]),
-                                      target.bias if bool(entry["hasBias"]) else None,
-                                      backend=route).to(device=device)
-                _replaceNamedModule(model, name, repl)
-                names.append(name)
-                modules[name] = repl
-            state = torch.load(root / "state.pt", map_location=_moduleDevice(model),
-                               weights_only=True)
-            model.load_state_dict(state, strict=True)
-            model.elasticbit = _ModelElasticBit(
-                model, threshold=float(manifest["threshold"]), decodePolicy=policy,
-                compressedNames=names, skippedNames=tuple(manifest.get("skippedNames", ())),
-                optimizationProfiles=manifest.get("optimizationProfiles", {}))
-            return model
-
-
-__all__ = ["ElasticBit", "RuntimeMatrix", "BitAnalysis", "BitCandidate", "BackendInfo"]
+        policy = _checkPolicy(decodePolicy)
+        return _read_artifact(model, src, policy, route)
