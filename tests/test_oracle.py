@@ -134,3 +134,25 @@ def test_select_bits_torch_restatement_runs_on_cpu():
     assert 3 <= bits <= 16 and err <= 0.01
     if bits <= 15:
         assert np.abs(codes).max() <= O.qmax(bits)
+
+
+def test_reference_selection_trace_replays_on_host():
+    """The recorded reference selection (tests/golden/selection_trace_*.json) replays
+    on the host and agrees with the oracle's restatement run there: BASELINE
+    config 1 selects 10 / 9 / 8 bits at thresholds 0.005 / 0.01 / 0.02."""
+    import torch
+
+    from tests.test_ref_selection_trace import CASES, THRESHOLDS, _trace, reference_selection
+
+    rows, cols, wfn, cfn = CASES["config1_1536x384"]
+    trace = _trace(rows, cols, 32)
+    w = torch.from_numpy(wfn()).half()
+    calib = cfn()
+    picked = []
+    for thr in THRESHOLDS:
+        rb, rerr, rq, rs = reference_selection(trace, w, calib, thr)
+        ob, oerr, oq, os_ = O.select_bits_torch(w, calib, thr)
+        assert (rb, rerr) == (ob, oerr)
+        assert np.array_equal(rq.numpy(), oq) and np.array_equal(rs.numpy(), os_)
+        picked.append(rb)
+    assert picked == [10, 9, 8]
