@@ -209,6 +209,21 @@ EBX_API ebx_status ebx_elastic_linear_packed(const void* x, int32_t x_dtype, int
 EBX_API ebx_status ebx_linear_swiglu(const ebx_matrix* m, const void* x, int64_t M, const void* bias,
                                      void* y, float* y32, void* stream);
 
+/* Several matrices that read the same activations -- Q, K and V projections,
+ * or gate and up -- each with its own storage width, scales, execution
+ * semantics and bias, in ONE decode launch: ys[i][M, rows_i] = x[M, cols] *
+ * W_i^T (+ biases[i]), i < count.  Replaces the reference's fused multi-matrix
+ * execution, which concatenates the dequantised FP16 weights of such a group
+ * into one matrix for a single GEMM (mlbricks/elasticbit/stage2f.py:382-420);
+ * here the codes stay at their own widths.  1 <= count <= 4, 0 <= M <= 16,
+ * every matrix on one device with the same cols; biases, y32s (and their
+ * entries) may be NULL.  EBX_ERR_UNSUPPORTED (nothing launched) unless every
+ * storage width is 8..12, cols % 64 == 0 and x is 16-byte aligned: run such
+ * matrices with ebx_linear. */
+EBX_API ebx_status ebx_linear_multi(const ebx_matrix* const* mats, int32_t count, const void* x,
+                                    int64_t M, const void* const* biases, void* const* ys,
+                                    float* const* y32s, void* stream);
+
 /* ---- Tensor-parallel exchange (row-parallel linear + all-reduce) ----------
  * No reference counterpart: the reference has no distributed code.  These
  * replace "row-parallel shard GEMV, then an NCCL all-reduce of the fp32

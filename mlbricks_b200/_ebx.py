@@ -74,6 +74,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ebx_device_status": (_ST, [_I32, ctypes.POINTER(_I32), _I32]),
     "ebx_fnv1a64": (_U64, [_P, _U64]),
     "ebx_linear_swiglu": (_ST, [_P, _P, _I64, _P, _P, _P, _P]),
+    "ebx_linear_multi": (_ST, [_P, _I32, _P, _I64, _P, _P, _P, _P]),
     "ebx_exchange_create": (_ST, [_I32, _I32, _I32, _I64, _I64, _P, ctypes.POINTER(_P)]),
     "ebx_exchange_connect": (_ST, [_P, _P]),
     "ebx_exchange_destroy": (_ST, [_P]),

@@ -431,6 +431,49 @@ ebx_status ebx_linear_swiglu(const ebx_matrix* h, const void* x, int64_t M, cons
     return EBX_OK;
 }
 
+ebx_status ebx_linear_multi(const ebx_matrix* const* mats, int32_t count, const void* x, int64_t M,
+                            const void* const* biases, void* const* ys, float* const* y32s,
+                            void* stream) {
+    if (!mats || !ys || count < 1 || (M > 0 && !x)) {
+        set_error("null argument");
+        return EBX_ERR_INVALID;
+    }
+    if (count > 4) {
+        set_error("ebx_linear_multi: at most 4 matrices per launch");
+        return EBX_ERR_INVALID;
+    }
+    if (M < 0 || M > 16) {
+        set_error("ebx_linear_multi: need 0 <= M <= 16 (decode batches)");
+        return EBX_ERR_INVALID;
+    }
+    const ebx::Matrix* ms[4];
+    for (int i = 0; i < count; ++i) {
+        if (!mats[i] || !ys[i]) {
+            set_error("null argument");
+            return EBX_ERR_INVALID;
+        }
+        ms[i] = &mats[i]->m;
+        if (ms[i]->cols != ms[0]->cols || ms[i]->device != ms[0]->device) {
+            set_error("ebx_linear_multi: every matrix must have the same cols and device");
+            return EBX_ERR_INVALID;
+        }
+    }
+    if (M == 0) return EBX_OK;
+    for (int i = 0; i < count; ++i) {
+        if (!ebx::multi_supported(*ms[i]) || (reinterpret_cast<uintptr_t>(x) & 15) != 0) {
+            set_error("ebx_linear_multi: one launch needs storage widths 8..12, cols % 64 == 0 and "
+                      "16-byte aligned x; run these matrices with ebx_linear");
+            return EBX_ERR_UNSUPPORTED;
+        }
+    }
+    DeviceGuard g(ms[0]->device);
+    EBX_CUDA(ebx::launch_decode_multi(ms, count, static_cast<const uint16_t*>(x), M,
+                                      reinterpret_cast<const uint16_t* const*>(biases),
+                                      reinterpret_cast<uint16_t* const*>(ys), y32s,
+                                      static_cast<cudaStream_t>(stream)));
+    return EBX_OK;
+}
+
 ebx_status ebx_device_status(int32_t device, int32_t* status, int32_t clear) {
     if (!status) {
         set_error("null argument");

@@ -56,6 +56,7 @@ struct DecodeArgs {
     int stage_bytes;  // pipe kernel: RG weight rounds + (min(M, 8 NT) + 1) activation rows
     XchgArgs xa;      // world > 0: fp32 partials go to the tensor-parallel exchange
     int act;          // 1: SwiGLU over interleaved gate/up rows (y has N / 2 columns)
+    int code;         // multi launch: 2 * bits + (integer semantics), selects the decode
     int pdl_early;    // pipe kernel: signal dependents at the start instead of the end
 };
 
@@ -370,10 +371,10 @@ __device__ __forceinline__ void pdl_trigger() {
 template <int B, bool HW, int NT, int TPW, int RG, bool XG, class S>
 __device__ __forceinline__ void plane_consume(const DecodeArgs& a, uint8_t* smem, uint32_t full0,
                                               uint32_t empty0, int rounds, int mrows, int warp,
-                                              int lane, float* red) {
+                                              int lane, float* red, int cta) {
     const int rgl = warp / kWarps;  // local row group (RG > 1: the groups share each activation stage)
     const int wt = warp % kWarps;   // tile slot within the round
-    const int g = blockIdx.x * RG + rgl;
+    const int g = cta * RG + rgl;
     const bool grp_ok = g < a.groups;
     const int r0 = lane >> 2;
     const int c = lane & 3;
@@ -529,8 +530,10 @@ __device__ __forceinline__ void plane_consume(const DecodeArgs& a, uint8_t* smem
 // traffic per weight falls by RG.  Requires K % 64 == 0 (the generic kernel
 // covers the rest); activation rows of tokens >= M are zeroed once and never
 // written by the copy engine, so the fragment loads need no predicates.
-template <int B, bool HW, int NT, bool DIRECT, int RG, int MINB, int TPW, bool XG = false>
-__global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(DecodeArgs a) {
+// The pipe decode of CTA `cta` of a launch over one matrix (decode_pipe_kernel: cta =
+// blockIdx.x; decode_multi_kernel: the CTA's index within its matrix's row groups).
+template <int B, bool HW, int NT, bool DIRECT, int RG, int TPW, bool XG = false>
+__device__ __forceinline__ void decode_pipe_body(const DecodeArgs& a, const int cta) {
     using S = PipeStage<B, NT, RG, TPW>;
     constexpr int kConsumers = kWarps * RG;
     // plane layout (b = 9..12), and b = 8's byte codes under integer semantics
@@ -571,7 +574,7 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
         // activation slices after it.
         int ngroups = 0;
 #pragma unroll
-        for (int rg = 0; rg < RG; ++rg) ngroups += (blockIdx.x * RG + rg) < a.groups ? 1 : 0;
+        for (int rg = 0; rg < RG; ++rg) ngroups += (cta * RG + rg) < a.groups ? 1 : 0;
         auto weights = [&](int r, int st) {
             const int ntile = min(S::kRound, a.kt - r * S::kRound);
             const uint32_t xbytes = uint32_t(ntile * kKTile * 2);
@@ -582,7 +585,7 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
                                         (XG ? 0u : xbytes * uint32_t(mrows)));
 #pragma unroll
                 for (int rg = 0; rg < RG; ++rg) {
-                    const int g = blockIdx.x * RG + rg;
+                    const int g = cta * RG + rg;
                     if (g < a.groups)
                         bulk_g2s(smem_u32(dst + rg * S::kWBytes),
                                  a.tiles + (size_t(g) * a.kt + size_t(r) * S::kRound) * S::kTileBytes,
@@ -618,12 +621,12 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
         // ---------------- consumer warps ----------------
       if constexpr (kPlane) {
         plane_consume<B, HW, NT, TPW, RG, XG, S>(a, smem, smem_u32(&full[0]), smem_u32(&empty[0]),
-                                                 rounds, mrows, warp, lane, red);
+                                                 rounds, mrows, warp, lane, red, cta);
         if (!a.pdl_early) pdl_trigger();
       } else {
         const int rgl = warp / kWarps;   // local row group
         const int wt = warp % kWarps;    // tile slot within the round
-        const int g = blockIdx.x * RG + rgl;
+        const int g = cta * RG + rgl;
         const bool grp_ok = g < a.groups;
         const int r0 = lane >> 2;
         const int c = lane & 3;
@@ -806,7 +809,7 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
         const int rgl = idx / (NT * 128);
         const int rem = idx % (NT * 128);
         const int nb = rem >> 7, l = (rem >> 2) & 31, i = rem & 3;
-        const int g = blockIdx.x * RG + rgl;
+        const int g = cta * RG + rgl;
         float v = 0.0f;
 #pragma unroll
         for (int ww = 0; ww < kWarps; ++ww) v += red[(((rgl * kWarps + ww) * NT + nb) * 32 + l) * 4 + i];
@@ -840,13 +843,18 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
             const int rgl = idx / (NT * 128);
             const int rem = idx % (NT * 128);
             const int nb = rem >> 7, l = (rem >> 2) & 31, i = rem & 3;
-            const int g = blockIdx.x * RG + rgl;
+            const int g = cta * RG + rgl;
             const int row = g * kRowGroup + (l >> 2) + 8 * (i >> 1);
             const int tok = 8 * nb + (l & 3) * 2 + (i & 1);
             if (g < a.groups && row < a.N && tok < a.M) xchg_finish_one(a, xe, tok, row);
         }
         xchg_advance(a.xa, xe);
     }
+}
+
+template <int B, bool HW, int NT, bool DIRECT, int RG, int MINB, int TPW, bool XG = false>
+__global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(DecodeArgs a) {
+    decode_pipe_body<B, HW, NT, DIRECT, RG, TPW, XG>(a, int(blockIdx.x));
 }
 
 constexpr int kStages = 4;
@@ -961,6 +969,89 @@ cudaError_t launch_pipe(DecodeArgs& a, int groups, cudaStream_t s) {
                              true);
 }
 
+// ---------------------------------------------------------------------------
+// Several matrices over the same activations in one launch
+// ---------------------------------------------------------------------------
+// The grid is the concatenation of every matrix's row-group CTAs; a CTA finds its
+// matrix from the prefix of CTA counts and runs that matrix's pipe decode (its own
+// width, scales, semantics, ring depth and outputs).  Widths 8..12 (the plane
+// decode, and b = 8's byte codes) are compiled in; anything else takes separate
+// launches.
+constexpr int kMaxMulti = 4;
+
+struct MultiArgs {
+    DecodeArgs m[kMaxMulti];
+    int first_cta[kMaxMulti + 1];
+    int count;
+};
+
+template <int NT, int TPW>
+__device__ __forceinline__ void multi_body(const DecodeArgs& a, int cta) {
+    switch (a.code) {
+#define EBX_MULTI_CASE(BB)                                                     \
+    case 2 * BB:                                                               \
+        decode_pipe_body<BB, false, NT, false, 1, TPW>(a, cta);                \
+        break;                                                                 \
+    case 2 * BB + 1:                                                           \
+        decode_pipe_body<BB, true, NT, false, 1, TPW>(a, cta);                 \
+        break;
+        EBX_MULTI_CASE(8) EBX_MULTI_CASE(9) EBX_MULTI_CASE(10) EBX_MULTI_CASE(11) EBX_MULTI_CASE(12)
+#undef EBX_MULTI_CASE
+        default:
+            break;
+    }
+}
+
+template <int NT, int TPW, int MINB>
+__global__ void __launch_bounds__(kThreads + 32, MINB) decode_multi_kernel(const __grid_constant__ MultiArgs ma) {
+    int j = 0;
+    while (j + 1 < ma.count && int(blockIdx.x) >= ma.first_cta[j + 1]) ++j;
+    multi_body<NT, TPW>(ma.m[j], int(blockIdx.x) - ma.first_cta[j]);
+}
+
+template <int NT, int TPW, int MINB>
+cudaError_t launch_multi(MultiArgs& ma, int total_ctas, int max_kt, cudaStream_t s) {
+    constexpr int kBudget = MINB == 3 ? 74 * 1024 : 110 * 1024;
+    constexpr int kFixed = 2 * kMaxStages * 8 + kWarps * NT * 128 * 4 + 16;
+    int smem = 0;
+    for (int i = 0; i < ma.count; ++i) {
+        DecodeArgs& a = ma.m[i];
+        const int bits = a.code / 2;
+        const int mrows = a.M < NT * 8 ? a.M : NT * 8;
+        const int wbytes = kWarps * TPW * bits * 128;
+        const int xstride = kWarps * TPW * kKTile * 2 + 16;
+        a.stage_bytes = wbytes + (mrows + 1) * xstride;
+        int D = (kBudget - kFixed) / a.stage_bytes;
+        D = D > kMaxStages ? kMaxStages : D;
+        if (D < 2) return cudaErrorInvalidConfiguration;
+        a.stages = D;
+        const int need = D * a.stage_bytes + kFixed;
+        smem = need > smem ? need : smem;
+    }
+    auto kern = decode_multi_kernel<NT, TPW, MINB>;
+    static std::atomic<uint64_t> configured{0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(configured.load(std::memory_order_relaxed) & bit)) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kBudget);
+        if (e != cudaSuccess) return e;
+        configured.fetch_or(bit);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(total_ctas));
+    cfg.blockDim = dim3(kThreads + 32);
+    cfg.dynamicSmemBytes = size_t(smem);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = max_kt <= 128 ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, ma);
+}
+
 template <int B, bool HW>
 cudaError_t dispatch_nt(DecodeArgs& a, int groups, bool pipe, bool direct, cudaStream_t s) {
     constexpr bool kPlane = plane_layout(B) || (B == 8 && HW);
@@ -1037,6 +1128,45 @@ cudaError_t dispatch_nt(DecodeArgs& a, int groups, bool pipe, bool direct, cudaS
 }
 
 }  // namespace
+
+bool multi_supported(const Matrix& m) {
+    return m.bits >= 8 && m.bits <= 12 && (m.cols % 64) == 0;
+}
+
+cudaError_t launch_decode_multi(const Matrix* const* ms, int count, const uint16_t* x, int64_t M,
+                                const uint16_t* const* bias, uint16_t* const* y,
+                                float* const* y32, cudaStream_t s) {
+    if (count < 1 || count > kMaxMulti || M < 1 || M > 16) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) != 0) return cudaErrorInvalidValue;
+    MultiArgs ma = {};
+    ma.count = count;
+    int total = 0, max_kt = 0;
+    for (int i = 0; i < count; ++i) {
+        const Matrix& m = *ms[i];
+        if (!multi_supported(m) || m.cols != ms[0]->cols) return cudaErrorInvalidValue;
+        DecodeArgs& a = ma.m[i];
+        a.tiles = m.tiles;
+        a.scales = m.scales;
+        a.x = x;
+        a.bias = bias ? bias[i] : nullptr;
+        a.y = y[i];
+        a.y32 = y32 ? y32[i] : nullptr;
+        a.M = int(M);
+        a.N = m.rows;
+        a.K = m.cols;
+        a.kt = int(m.kt);
+        a.groups = int(m.groups);
+        a.magic = 0x4B000000u;
+        a.magic_plane = 0x64646464u;
+        a.code = 2 * m.bits + ((m.exec_width < 16 && m.bits <= 12) ? 1 : 0);
+        ma.first_cta[i] = total;
+        total += int(m.groups);
+        max_kt = int(m.kt) > max_kt ? int(m.kt) : max_kt;
+    }
+    ma.first_cta[count] = total;
+    return M <= 8 ? launch_multi<1, 2, 2>(ma, total, max_kt, s)
+                  : launch_multi<2, 1, 2>(ma, total, max_kt, s);
+}
 
 cudaError_t read_device_status(int* status, bool clear, cudaStream_t s) {
     cudaError_t e = cudaMemcpyFromSymbolAsync(status, g_device_status, sizeof(int), 0,

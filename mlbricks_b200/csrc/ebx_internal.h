@@ -69,6 +69,13 @@ struct XchgArgs {
 cudaError_t launch_decode(const Matrix& m, const uint16_t* x, int64_t M, const uint16_t* bias,
                           uint16_t* y, float* y32, cudaStream_t s, XchgArgs* xa = nullptr,
                           int act = 0);
+// Several matrices reading the same x [M, cols] (M <= 16) in one launch; each keeps
+// its own width (8..12), scales, semantics, bias and outputs (bias / y32 entries may
+// be null, bias and y32 arrays themselves may be null).
+bool multi_supported(const Matrix& m);
+cudaError_t launch_decode_multi(const Matrix* const* ms, int count, const uint16_t* x, int64_t M,
+                                const uint16_t* const* bias, uint16_t* const* y,
+                                float* const* y32, cudaStream_t s);
 // Reads (and optionally clears) the device-side status word that bounded
 // waits set on timeout (0 = healthy).  Synchronizes `s`.
 cudaError_t read_device_status(int* status, bool clear, cudaStream_t s);

@@ -398,6 +398,43 @@ class RuntimeMatrix:
         self._launch(xc, M, b, y, y32)
         return (y, y32) if out32 else y
 
+    @staticmethod
+    def linear_multi(mats: "list[RuntimeMatrix]", x: torch.Tensor,
+                     biases: "list[torch.Tensor | None] | None" = None) -> list[torch.Tensor]:
+        """y_i = x @ W_i^T (+ b_i) for matrices that share x, in one decode launch
+        (ebx_linear_multi) when x has at most 16 rows and every width is 8..12;
+        otherwise one ebx_linear launch per matrix."""
+        if not mats:
+            return []
+        first = mats[0]
+        if x.dtype != torch.float16 or not x.is_cuda or x.shape[-1] != first._cols:
+            raise ValueError("linear_multi requires FP16 CUDA activations of the matrices' width")
+        biases = list(biases) if biases is not None else [None] * len(mats)
+        xc = x if x.is_contiguous() else x.contiguous()
+        M = xc.numel() // first._cols
+        if 0 < M <= 16 and len(mats) <= 4 and all(m._cols == first._cols and
+                                                  m._device == first._device for m in mats):
+            ys = [torch.empty((*x.shape[:-1], m._rows), dtype=torch.float16, device=x.device)
+                  for m in mats]
+            bs = []
+            for m, b in zip(mats, biases):
+                if b is not None:
+                    b = b.detach().to(device=x.device, dtype=torch.float16).contiguous()
+                    if b.numel() != m._rows:
+                        raise ValueError("bias must match output features")
+                bs.append(b)
+            n = len(mats)
+            hs = (ctypes.c_void_p * n)(*[m._h.value for m in mats])
+            yp = (ctypes.c_void_p * n)(*[y.data_ptr() for y in ys])
+            bp = (ctypes.c_void_p * n)(*[None if b is None else b.data_ptr() for b in bs])
+            st = _LIB.ebx_linear_multi(hs, n, xc.data_ptr(), M, bp, yp, None,
+                                       _ebx.stream_ptr(device=first._device))
+            if st == _ebx.EBX_OK:
+                return ys
+            if st != _ebx.EBX_ERR_UNSUPPORTED:
+                _ebx.check(st)
+        return [m.linear(xc, b) for m, b in zip(mats, biases)]
+
     def linear_swiglu(self, x: torch.Tensor, bias: torch.Tensor | None = None,
                       out32: bool = False):
         """fp16(silu(g) * u) for a matrix whose gate/up rows are interleaved in blocks of 8

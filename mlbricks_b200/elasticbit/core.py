@@ -332,6 +332,53 @@ def _row_regime(rows: int) -> str:
     return "small-batch" if rows <= 256 else "prefill"
 
 
+class _FusedGroup:
+    """Compressed Linears that read the same input tensor (Q, K and V; gate and up).
+
+    At decode sizes (at most 16 rows) the first member called with an input runs
+    every member in ONE launch (ebx_linear_multi: each matrix keeps its own
+    width, scales and semantics) and keeps the other members' outputs until they
+    are asked for with that same input object (same tensor, same version, same
+    stream).  Any other call runs on its own.  Used only while every member is on
+    the native route for decode sizes, so the arithmetic is the one each member
+    would run alone.  This replaces the reference's fused execution, which
+    concatenates the groups' dequantised FP16 weights (stage2f.py:382-420).
+    """
+
+    def __init__(self, layers: Sequence["_ElasticLinear"]) -> None:
+        self.layers = list(layers)
+        self._key: tuple | None = None
+        self._x: torch.Tensor | None = None
+        self._outputs: dict[int, torch.Tensor] = {}
+
+    def _native_decode(self, layer: "_ElasticLinear") -> bool:
+        if layer.backend == "native":
+            return True
+        if layer.backend != "auto":
+            return False
+        routes = getattr(layer, "_mlbricks_frozen_auto_routes", None) or {}
+        return routes.get(("elastic_linear", False, "decode")) == "native"
+
+    def serves(self, x: torch.Tensor) -> bool:
+        rows = x.numel() // max(1, x.shape[-1])
+        return 0 < rows <= 16 and all(self._native_decode(layer) for layer in self.layers)
+
+    def output(self, layer: "_ElasticLinear", x: torch.Tensor) -> torch.Tensor:
+        key = (x._version, torch.cuda.current_stream(x.device).cuda_stream)
+        if self._x is not x or self._key != key or id(layer) not in self._outputs:
+            natives = [getattr(m.matrix, "_native", m.matrix) for m in self.layers]
+            biases = [m._bias_for(x) for m in self.layers]
+            x2 = x.reshape(-1, x.shape[-1])
+            ys = type(natives[0]).linear_multi(natives, x2, biases)
+            self._outputs = {id(m): y.view(*x.shape[:-1], m.outFeatures)
+                             for m, y in zip(self.layers, ys)}
+            self._x, self._key = x, key
+        y = self._outputs.pop(id(layer))
+        if not self._outputs:  # every member served: drop the input reference
+            self._x = self._key = None
+        return y
+
+
 class _ElasticLinear(nn.Module):
     """Internal replacement for nn.Linear.  Not part of the public import surface.
 
@@ -352,6 +399,7 @@ class _ElasticLinear(nn.Module):
         self.inFeatures = int(inFeatures)
         self.outFeatures = int(outFeatures)
         self.backend = normalize_backend(backend)
+        self._fused: _FusedGroup | None = None  # siblings reading the same input (compress)
         if bias is None:
             self.register_parameter("bias", None)
         else:
@@ -386,6 +434,9 @@ class _ElasticLinear(nn.Module):
         eligible = x.is_cuda and x.dtype == torch.float16
         if not eligible or self.backend == "pytorch":
             return self._forward_pytorch(x)
+        group = self._fused
+        if group is not None and group.serves(x):
+            return group.output(self, x)
         if self.backend == "native":
             return self._forward_native(x)
         from ..planner import EXECUTION_PLANNER
@@ -509,11 +560,13 @@ class _RowRecorder:
         self.limit = int(limit)
         self._rows: dict[str, list[torch.Tensor]] = {}
         self._count: dict[str, int] = {}
+        self._first: dict[str, torch.Tensor] = {}  # the input object of each name's first call
 
     def _pre_hook(self, name: str):
         def record(_module: nn.Module, inputs: tuple[Any, ...]) -> None:
             if not inputs or not torch.is_tensor(inputs[0]):
                 return
+            self._first.setdefault(name, inputs[0])  # held, so its id stays unique
             room = self.limit - self._count.get(name, 0)
             if room <= 0:
                 return
@@ -543,6 +596,17 @@ class _RowRecorder:
     def release(self, names: Sequence[str]) -> None:
         for n in names:
             self._rows.pop(n, None)
+
+    def siblings(self, names: Sequence[str]) -> list[list[str]]:
+        """Groups (2..4 names, in `names` order) whose first call received the very
+        same input tensor object."""
+        by_input: dict[int, list[str]] = {}
+        for n in names:
+            x = self._first.get(n)
+            if x is not None:
+                by_input.setdefault(id(x), []).append(n)
+        self._first.clear()
+        return [g for g in by_input.values() if 2 <= len(g) <= 4]
 
 
 @dataclass
@@ -808,6 +872,15 @@ class ElasticBit:
             del module, matrix, rows
             gc.collect()
             torch.cuda.empty_cache()
+
+        # siblings that read one input share a fused decode launch
+        done = set(compressed)
+        for names in recorder.siblings([n for g in work for n in g.names]):
+            if all(n in done for n in names):
+                layers = [model.get_submodule(n) for n in names]
+                group = _FusedGroup(layers)
+                for layer in layers:
+                    layer._fused = group
 
         model.elasticbit = _ModelElasticBit(model, threshold=thr, decodePolicy=policy,
                                             compressedNames=compressed, skippedNames=skipped)
