@@ -112,9 +112,14 @@ EBX_API ebx_status ebx_matrix_export_scales(const ebx_matrix* m, float* dst, voi
  * (cu:982-1022) and the values of RuntimeMatrix.dequantize (cu:208-238). */
 EBX_API ebx_status ebx_matrix_materialize(const ebx_matrix* m, void* dst, void* stream);
 
-/* Workspace bytes ebx_linear needs for M activation rows (0 when none): the
- * decode-GEMM's fp32 split-K partials for 16 < M <= 128 (and M <= 256 when
- * cols >= 8192), the exactly dequantised fp16 weight for larger M. */
+/* Workspace bytes ebx_linear asks for with M activation rows (0 when none):
+ * the decode-GEMM's fp32 split-K partials for 16 < M <= 256 (required when
+ * nonzero), and for larger M room for the exactly dequantised fp16 weight --
+ * optional: with it the prefill takes materialise + tcgen05 GEMM (the faster
+ * route; fp16(q*s) operands, the reference's prefill arithmetic, whatever the
+ * execution width), without it (NULL or smaller) the prefill decode-GEMM, which
+ * decodes the codes into shared memory per k-block, needs no memory at all and
+ * keeps the execution width's semantics. */
 EBX_API uint64_t ebx_linear_workspace_bytes(const ebx_matrix* m, int64_t M);
 
 /* y[M, rows] = x[M, cols] * W^T (+ bias), all fp16 DEVICE pointers, row-major,
@@ -122,9 +127,10 @@ EBX_API uint64_t ebx_linear_workspace_bytes(const ebx_matrix* m, int64_t M);
  * the fp32 value that was rounded into y.  Replaces _ElasticLinear.forward's
  * two routes (core.py:446-471): RuntimeMatrix.forwardTorch (cu:902-931) for
  * M = 1 and materialise + F.linear for M > 1.  Routes by M: the decode kernel
- * (M <= 16, in 16-row launches up to M = 64 where the decode-GEMM does not
- * apply), the decode-GEMM (codes decoded into tcgen05 tiles), or materialise +
- * tcgen05 GEMM; workspace as ebx_linear_workspace_bytes says. */
+ * (M <= 16, in 16-row launches where the decode-GEMM does not apply), the
+ * decode-GEMM (16 < M <= 256: codes decoded into tcgen05 tiles), and for larger
+ * M materialise + tcgen05 GEMM (given the optional workspace) or the prefill
+ * decode-GEMM; workspace as ebx_linear_workspace_bytes says. */
 EBX_API ebx_status ebx_linear(const ebx_matrix* m, const void* x, int64_t M, const void* bias, void* y,
                       float* y32, void* workspace, uint64_t workspace_bytes, void* stream);
 

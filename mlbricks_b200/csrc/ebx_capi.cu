@@ -354,11 +354,12 @@ ebx_status ebx_matrix_materialize(const ebx_matrix* h, void* dst, void* stream) 
 
 uint64_t ebx_linear_workspace_bytes(const ebx_matrix* h, int64_t M) {
     // 16 < M <= 256: the decode-GEMM's fp32 split-K partials (when K is split);
-    // M > 256: room for the exactly dequantised fp16 weight fed to the tensor-core
-    // GEMM; M <= 16 runs the decode kernel and needs nothing.
+    // M <= 16: nothing (decode kernel).
     if (!h || M <= ebx::kDgemmMinRows || (h->m.cols % 8) != 0) return 0;
     if (M <= ebx::kDgemmMaxRows && ebx::dgemm_route(h->m, M)) return ebx::dgemm_workspace_bytes(h->m, M);
-    if (M <= ebx::kGemmMinRows) return 0;  // chunked decode
+    // larger M: optional room for the exactly dequantised fp16 weight, which takes the
+    // materialise + tcgen05 GEMM route (faster); without it the prefill decode-GEMM runs
+    if (M <= ebx::kGemmMinRows) return 0;
     return uint64_t(ebx::round_up(int64_t(h->m.rows) * h->m.cols * 2, 256));
 }
 
@@ -389,18 +390,23 @@ ebx_status ebx_linear(const ebx_matrix* h, const void* x, int64_t M, const void*
                                    workspace, workspace_bytes, s));
         return EBX_OK;
     }
-    if (M > ebx::kGemmMinRows && need > 0 && ebx::gemm_supported(h->m.cols, x, workspace)) {
-        // prefill: exact fp16 weight into the workspace, then the tcgen05 GEMM
-        const uint64_t w16_bytes = uint64_t(ebx::round_up(int64_t(h->m.rows) * h->m.cols * 2, 256));
-        if (!workspace || workspace_bytes < w16_bytes) {
-            set_error("ebx_linear: workspace missing or smaller than ebx_linear_workspace_bytes()");
-            return EBX_ERR_WORKSPACE;
-        }
+    const uint64_t w16_bytes = uint64_t(ebx::round_up(int64_t(h->m.rows) * h->m.cols * 2, 256));
+    if (M > ebx::kGemmMinRows && need > 0 && workspace && workspace_bytes >= w16_bytes &&
+        ebx::gemm_supported(h->m.cols, x, workspace)) {
+        // prefill with the optional workspace: exact fp16 weight into it, then the tcgen05 GEMM
         uint16_t* w16 = static_cast<uint16_t*>(workspace);
         EBX_CUDA(ebx::launch_materialize(h->m, w16, s));
         EBX_CUDA(ebx::launch_gemm_f16(static_cast<const uint16_t*>(x), w16, M, h->m.rows,
                                       h->m.cols, static_cast<const uint16_t*>(bias),
                                       static_cast<uint16_t*>(y), y32, s));
+        return EBX_OK;
+    }
+    if (M > ebx::kGemmMinRows && ebx::pgemm_supported(h->m, x)) {
+        // prefill without a workspace: tcgen05 GEMM with the codes decoded into shared
+        // memory per k-block
+        EBX_CUDA(ebx::launch_pgemm(h->m, static_cast<const uint16_t*>(x), M,
+                                   static_cast<const uint16_t*>(bias), static_cast<uint16_t*>(y), y32,
+                                   s));
         return EBX_OK;
     }
     EBX_CUDA(ebx::launch_decode(h->m, static_cast<const uint16_t*>(x), M,

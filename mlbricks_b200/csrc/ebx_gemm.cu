@@ -92,6 +92,16 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// 4-d tensor load (the code tiles of several row groups at one k-block; see make_code_map).
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            int c3, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2];\n" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+
 __device__ __forceinline__ void umma_f16(uint32_t tmem, uint64_t adesc, uint64_t bdesc,
                                          uint32_t idesc, uint32_t accumulate) {
     asm volatile(
@@ -316,6 +326,24 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
+// The tile layout of a matrix's codes as a 4-d uint8 tensor [groups][kt][b rows][128 B]
+// (dims innermost first: 128 bytes, b, kt, groups), with a box of `box_groups` row groups
+// at one k-tile: ONE TMA request brings the supertiles of that many row groups for one
+// k-block, landing contiguously (group after group) -- instead of one bulk copy per
+// row group.  Row groups past the matrix read as zeros (the box is always full).
+bool make_code_map(CUtensorMap* map, const Matrix& m, int box_groups) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t tb = cuuint64_t(tile_bytes(m.bits));
+    const cuuint64_t dims[4] = {128, cuuint64_t(m.bits), cuuint64_t(m.kt), cuuint64_t(m.groups)};
+    const cuuint64_t strides[3] = {128, tb, tb * cuuint64_t(m.kt)};
+    const cuuint32_t box[4] = {128, cuuint32_t(m.bits), 1, cuuint32_t(box_groups)};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<uint8_t*>(m.tiles), dims, strides, box,
+              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Row-major fp16 [rows, K] tensor map with a (64 x box_rows) box, 128 B swizzle.
 bool make_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows) {
     auto fn = encode_fn();
@@ -435,7 +463,8 @@ __device__ __forceinline__ void dg_decode(const uint32_t (&w)[B], const uint64_t
 
 template <int B, bool HW>
 __global__ void __launch_bounds__(kDgThreads, 2)
-    dgemm_kernel(const __grid_constant__ CUtensorMap tma_x, DgArgs a) {
+    dgemm_kernel(const __grid_constant__ CUtensorMap tma_x, const __grid_constant__ CUtensorMap tma_c,
+                 DgArgs a) {
     constexpr int kCodeBytes = B * 128;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -491,13 +520,13 @@ __global__ void __launch_bounds__(kDgThreads, 2)
             const uint32_t bar = smem_u32(&full[st]);
             uint8_t* stage = smem + st * SB;
             if (lane == 0) {
-                mbar_expect_tx(bar, uint32_t(ngroups * kCodeBytes + a.mp * BK * 2));
+                // one request for all 8 row groups' supertiles (full box: groups past
+                // the matrix read as zeros)
+                mbar_expect_tx(bar, uint32_t(kDgGroups * kCodeBytes + a.mp * BK * 2));
                 tma_load_2d(smem_u32(stage + a.b_off), &tma_x, kb * BK, 0, bar);
+                tma_load_4d(smem_u32(stage + a.c_off), &tma_c, 0, 0, kb, g0, bar);
             }
             __syncwarp();
-            if (lane < ngroups)
-                bulk_g2s(smem_u32(stage + a.c_off + lane * kCodeBytes),
-                         a.tiles + (size_t(g0 + lane) * a.kt + kb) * kCodeBytes, kCodeBytes, bar);
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -672,6 +701,335 @@ __global__ void dgemm_reduce_kernel(const float* part, int S, int M, int N, cons
     if (y32) y32[i0] = v;
 }
 
+// ---------------------------------------------------------------------------
+// Prefill decode-GEMM (larger M): the codes decoded straight into the B tile
+// ---------------------------------------------------------------------------
+// The persistent structure of gemm_f16_kernel (output tiles of 128 tokens x 256
+// weight rows, two TMEM accumulators so the epilogue of one tile runs under the
+// MMAs of the next), but the weight operand never exists in HBM as FP16: per
+// 64-k block the producer copies the 16 row groups' exact-width supertiles
+// (b x 128 bytes each, one 4-d TMA request) next to the TMA-loaded x tile (a
+// D-stage load ring); sixteen decoding warps, one row group each, turn them into
+// the K-major, 128-byte-swizzled fp16 B tile in one of two B buffers, one
+// k-block ahead of the MMAs (the decode kernel's
+// arithmetic: integer codes under integer-code semantics -- the row scale is
+// applied in the epilogue -- or fp16_rn(fp32_rn(q * s)) under fullPrecision)
+// and the MMA thread consumes it.  No workspace, one HBM pass over the codes per
+// concurrently resident token-tile row; the x and code tiles of a raster group
+// of token tiles stay L2-resident.
+constexpr int kPgBN = 256;                                 // weight rows per tile (MMA N)
+constexpr int kPgGroups = kPgBN / kRowGroup;               // 16 row groups
+constexpr int kPgDecoders = 16;                            // one row group each
+constexpr int kPgThreads = 32 * (2 + 4 + kPgDecoders);     // producer, MMA, epilogue x4, decoders
+constexpr int kPgBBytes = kPgBN * BK * 2;                  // 32 KB decoded tile
+constexpr uint32_t kPgIdesc = (1u << 4) | (uint32_t(kPgBN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+
+struct PgArgs {
+    const uint8_t* tiles;
+    const float* scales;
+    const uint16_t* bias;
+    uint16_t* y;
+    float* y32;
+    int M, N, kt, groups;
+    int stages, stage_bytes;  // load-ring stage: [x tile | codes]; two B tiles follow the ring
+};
+
+__device__ __forceinline__ bool pg_wait(uint32_t bar, uint32_t parity) {
+    if (mbar_wait_bounded(bar, parity)) return true;
+    atomicExch(&g_gemm_status, 0x7105);
+    return false;
+}
+
+template <int B, bool HW>
+__global__ void __launch_bounds__(kPgThreads, 1)
+    pgemm_kernel(const __grid_constant__ CUtensorMap tma_x, const __grid_constant__ CUtensorMap tma_c,
+                 PgArgs a) {
+    constexpr int kCodeBytes = B * 128;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    const int D = a.stages;
+    const int SB = a.stage_bytes;
+    uint8_t* btile = smem + D * SB;  // two decoded B tiles, 1024-aligned
+    uint64_t* full = reinterpret_cast<uint64_t*>(btile + 2 * kPgBBytes);
+    uint64_t* empty = full + D;
+    uint64_t* bready = empty + D;  // [2]: decoders -> MMA
+    uint64_t* bempty = bready + 2; // [2]: MMA -> decoders
+    uint64_t* acc_full = bempty + 2;
+    uint64_t* acc_empty = acc_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int m_tiles = (a.M + BM - 1) / BM;
+    const int n_tiles = (a.groups + kPgGroups - 1) / kPgGroups;
+    const int tiles = m_tiles * n_tiles;
+    const int kblocks = a.kt;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int i = 0; i < D; ++i) {
+                mbar_init(smem_u32(&full[i]), 1);
+                mbar_init(smem_u32(&empty[i]), 1);
+            }
+            for (int i = 0; i < 2; ++i) {
+                mbar_init(smem_u32(&bready[i]), kPgDecoders);
+                mbar_init(smem_u32(&bempty[i]), 1);
+                mbar_init(smem_u32(&acc_full[i]), 1);
+                mbar_init(smem_u32(&acc_empty[i]), 4);
+            }
+            fence_proxy_async_smem();
+        }
+        __syncwarp();
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(2 * kPgBN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- producer: x tile (TMA) + the 16 row groups' supertiles ----------------
+        int it = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+            int mt, nt;
+            tile_coords(t, m_tiles, n_tiles, mt, nt);
+            const int g0 = nt * kPgGroups;
+            const int ng = min(kPgGroups, a.groups - g0);
+            for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                const int st = it % D;
+                bool w_ok = true;
+                if (lane == 0 && it >= D) w_ok = pg_wait(smem_u32(&empty[st]), uint32_t(((it / D) - 1) & 1));
+                if (!__shfl_sync(0xffffffffu, w_ok ? 1 : 0, 0)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* stage = smem + st * SB;
+                const uint32_t bar = smem_u32(&full[st]);
+                if (lane == 0) {
+                    // the code box is always full (row groups past the matrix read as zeros)
+                    mbar_expect_tx(bar, uint32_t(kABytes + kPgGroups * kCodeBytes));
+                    tma_load_2d(smem_u32(stage), &tma_x, kb * BK, mt * BM, bar);
+                    tma_load_4d(smem_u32(stage + kABytes), &tma_c, 0, 0, kb, g0, bar);
+                }
+                __syncwarp();
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            int it = 0, i = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++i) {
+                const int acc = i & 1;
+                if (i >= 2 && !pg_wait(smem_u32(&acc_empty[acc]), uint32_t(((i >> 1) - 1) & 1))) break;
+                asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+                const uint32_t d = tmem + uint32_t(acc * kPgBN);
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int st = it % D;
+                    const int bb = it & 1;
+                    // x tile landed (the decoders also waited for it) and the B tile is decoded
+                    if (!pg_wait(smem_u32(&full[st]), uint32_t(it / D) & 1u) ||
+                        !pg_wait(smem_u32(&bready[bb]), uint32_t(it >> 1) & 1u)) {
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+                    const uint32_t abase = smem_u32(smem + st * SB);
+                    const uint32_t bbase = smem_u32(btile + bb * kPgBBytes);
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k)
+                        umma_f16(d, sw128_desc(abase + k * 32), sw128_desc(bbase + k * 32), kPgIdesc,
+                                 (kb | k) != 0 ? 1u : 0u);
+                    umma_commit(smem_u32(&empty[st]));
+                    umma_commit(smem_u32(&bempty[bb]));
+                }
+                umma_commit(smem_u32(&acc_full[acc]));
+            }
+        }
+        __syncwarp();
+    } else if (warp < 6) {
+        // ---------------- epilogue: TMEM lanes = tokens, columns = weight rows ----------------
+        const int quarter = warp & 3;
+        const bool vec = (a.N % 8) == 0;
+        int i = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+            const int acc = i & 1;
+            if (!pg_wait(smem_u32(&acc_full[acc]), uint32_t((i >> 1) & 1))) break;
+            asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+            int mt, nt;
+            tile_coords(t, m_tiles, n_tiles, mt, nt);
+            const int m = mt * BM + quarter * 32 + lane;
+            const int n0 = nt * kPgBN;
+#pragma unroll 1
+            for (int c = 0; c < kPgBN / 32; ++c) {
+                uint32_t v[32];
+                const uint32_t taddr =
+                    tmem + (uint32_t(quarter * 32) << 16) + uint32_t(acc * kPgBN + c * 32);
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+                    "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+                    : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
+                      "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]),
+                      "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]),
+                      "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+                      "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]),
+                      "=r"(v[30]), "=r"(v[31])
+                    : "r"(taddr));
+                asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+                const int nb = n0 + c * 32;
+                if (m >= a.M || nb >= a.N) continue;
+                float f[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    f[j] = __uint_as_float(v[j]);
+                    if (nb + j < a.N) {
+                        if constexpr (HW && B != kFp16Bits) f[j] *= a.scales[nb + j];
+                        if (a.bias) f[j] += __half2float(__ushort_as_half(a.bias[nb + j]));
+                    }
+                }
+                uint16_t* yrow = a.y + size_t(m) * a.N + nb;
+                if (vec && nb + 32 <= a.N) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        uint4 pk;
+                        pk.x = pack_half2(f[8 * q + 0], f[8 * q + 1]);
+                        pk.y = pack_half2(f[8 * q + 2], f[8 * q + 3]);
+                        pk.z = pack_half2(f[8 * q + 4], f[8 * q + 5]);
+                        pk.w = pack_half2(f[8 * q + 6], f[8 * q + 7]);
+                        reinterpret_cast<uint4*>(yrow)[q] = pk;
+                    }
+                    if (a.y32) {
+                        float* y32row = a.y32 + size_t(m) * a.N + nb;
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            reinterpret_cast<float4*>(y32row)[q] =
+                                make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        if (nb + j < a.N) {
+                            yrow[j] = __half_as_ushort(__float2half_rn(f[j]));
+                            if (a.y32) a.y32[size_t(m) * a.N + nb + j] = f[j];
+                        }
+                    }
+                }
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc]));
+        }
+    } else {
+        // ---------------- decoders: row groups dw and dw + 8 of the tile ----------------
+        const int dw = warp - 6;
+        const int r0 = lane >> 2;
+        const int c = lane & 3;
+        DgConsts<B> pk;
+        pk.init(0x4B000000u);
+        constexpr int kPer = kPgGroups / kPgDecoders;  // row groups per decoding warp
+        uint32_t off[kPer][4];  // swizzled 16-byte chunk offsets of this lane's rows, per group
+#pragma unroll
+        for (int h = 0; h < kPer; ++h) {
+            const int nlo = 16 * (dw + kPgDecoders * h) + r0, nhi = nlo + 8;
+            off[h][0] = uint32_t(nlo * 128 + (((2 * c) ^ (nlo & 7)) << 4));
+            off[h][1] = uint32_t(nlo * 128 + (((2 * c + 1) ^ (nlo & 7)) << 4));
+            off[h][2] = uint32_t(nhi * 128 + (((2 * c) ^ (nhi & 7)) << 4));
+            off[h][3] = uint32_t(nhi * 128 + (((2 * c + 1) ^ (nhi & 7)) << 4));
+        }
+        int it = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+            int mt, nt;
+            tile_coords(t, m_tiles, n_tiles, mt, nt);
+            const int g0 = nt * kPgGroups;
+            const int ng = min(kPgGroups, a.groups - g0);
+            uint64_t s2[kPer][2] = {};
+            if constexpr (B != kFp16Bits && !HW) {
+#pragma unroll
+                for (int h = 0; h < kPer; ++h)
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        const int gr = dw + kPgDecoders * h;
+                        const int row = (g0 + gr) * kRowGroup + r0 + 8 * q;
+                        const float sv = (gr < ng && row < a.N) ? a.scales[row] : 0.0f;
+                        s2[h][q] = pack2f(sv, sv);
+                    }
+            }
+            for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                const int st = it % D;
+                const int bb = it & 1;
+                if (!pg_wait(smem_u32(&full[st]), uint32_t(it / D) & 1u) ||
+                    (it >= 2 && !pg_wait(smem_u32(&bempty[bb]), uint32_t((it >> 1) - 1) & 1u))) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* stage = smem + st * SB;
+                const uint32_t bbase = smem_u32(btile + bb * kPgBBytes);
+#pragma unroll
+                for (int h = 0; h < kPer; ++h) {
+                    const int r = dw + kPgDecoders * h;
+                    if (r >= ng) continue;  // rows past N: their columns are never stored
+                    const uint8_t* cb = stage + kABytes + r * kCodeBytes;
+                    uint32_t w[B];
+#pragma unroll
+                    for (int q = 0; q < B / 4; ++q) {
+                        const uint4 v = *reinterpret_cast<const uint4*>(cb + q * 512 + lane * 16);
+                        w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
+                    }
+                    if constexpr ((B & 2) != 0) {
+                        const uint2 v = *reinterpret_cast<const uint2*>(cb + (B / 4) * 512 + lane * 8);
+                        w[4 * (B / 4)] = v.x;
+                        w[4 * (B / 4) + 1] = v.y;
+                    }
+                    if constexpr ((B & 1) != 0)
+                        w[B - 1] = *reinterpret_cast<const uint32_t*>(cb + (B / 4) * 512 +
+                                                                      ((B & 2) ? 256 : 0) + lane * 4);
+                    uint32_t af[16];
+                    dg_decode<B, HW>(w, s2[h], pk, af);
+                    sts128(bbase + off[h][0], af[0], af[2], af[4], af[6]);
+                    sts128(bbase + off[h][1], af[8], af[10], af[12], af[14]);
+                    sts128(bbase + off[h][2], af[1], af[3], af[5], af[7]);
+                    sts128(bbase + off[h][3], af[9], af[11], af[13], af[15]);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&bready[bb]));
+            }
+        }
+    }
+
+    asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem),
+                     "r"(2 * kPgBN)
+                     : "memory");
+    }
+}
+
+template <int B, bool HW>
+cudaError_t launch_pgemm_b(const CUtensorMap& tx, const CUtensorMap& tc, const PgArgs& a, unsigned grid,
+                           int smem, int dev, cudaStream_t s) {
+    auto kern = pgemm_kernel<B, HW>;
+    static std::atomic<uint64_t> configured{0};
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(configured.load(std::memory_order_relaxed) & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e != cudaSuccess) return e;
+        configured.fetch_or(bit);
+    }
+    kern<<<grid, kPgThreads, smem, s>>>(tx, tc, a);
+    return cudaGetLastError();
+}
+
 struct DgPlan {
     int S, kb_per, mp, tmem_cols, stages, stage_bytes, b_off, c_off, smem;
 };
@@ -722,8 +1080,8 @@ DgPlan dg_plan(const Matrix& m, int64_t M, int sms) {
 }
 
 template <int B, bool HW>
-cudaError_t launch_dgemm_b(const Matrix& m, const CUtensorMap& tx, const DgArgs& a, unsigned grid,
-                           int smem, int dev, cudaStream_t s) {
+cudaError_t launch_dgemm_b(const Matrix& m, const CUtensorMap& tx, const CUtensorMap& tc, const DgArgs& a,
+                           unsigned grid, int smem, int dev, cudaStream_t s) {
     auto kern = dgemm_kernel<B, HW>;
     static std::atomic<uint64_t> configured{0};
     const uint64_t bit = 1ull << (dev & 63);
@@ -732,7 +1090,7 @@ cudaError_t launch_dgemm_b(const Matrix& m, const CUtensorMap& tx, const DgArgs&
         if (e != cudaSuccess) return e;
         configured.fetch_or(bit);
     }
-    kern<<<grid, kDgThreads, smem, s>>>(tx, a);
+    kern<<<grid, kDgThreads, smem, s>>>(tx, tc, a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || a.S == 1) return e;
     const int64_t total = int64_t(a.M) * a.N;
@@ -750,6 +1108,58 @@ cudaError_t launch_dgemm_b(const Matrix& m, const CUtensorMap& tx, const DgArgs&
                               m.scales, a.bias, a.y, a.y32);
 }
 }  // namespace
+
+bool pgemm_supported(const Matrix& m, const void* x) {
+    return (m.cols % 8) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && encode_fn() != nullptr;
+}
+
+cudaError_t launch_pgemm(const Matrix& m, const uint16_t* x, int64_t M, const uint16_t* bias,
+                         uint16_t* y, float* y32, cudaStream_t s) {
+    if (M <= 0) return cudaSuccess;
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    CUtensorMap tx, tc;
+    if (M > INT32_MAX || !make_map(&tx, x, int(M), m.cols, BM) || !make_code_map(&tc, m, kPgGroups))
+        return cudaErrorInvalidValue;
+    PgArgs a{};
+    a.tiles = m.tiles;
+    a.scales = m.scales;
+    a.bias = bias;
+    a.y = y;
+    a.y32 = y32;
+    a.M = int(M);
+    a.N = m.rows;
+    a.kt = int(m.kt);
+    a.groups = int(m.groups);
+    a.stage_bytes = int(round_up(kABytes + kPgGroups * tile_bytes(m.bits), 1024));
+    constexpr int kOverhead = 1024 + 512;
+    int D = (227 * 1024 - kOverhead - 2 * kPgBBytes) / a.stage_bytes;
+    D = D > 8 ? 8 : D;
+    if (D < 2) return cudaErrorInvalidConfiguration;
+    a.stages = D;
+    const int smem = D * a.stage_bytes + 2 * kPgBBytes + kOverhead;
+    const int64_t tiles = ((M + BM - 1) / BM) * ((m.groups + kPgGroups - 1) / kPgGroups);
+    const unsigned grid = unsigned(tiles < sms ? tiles : sms);
+    const bool hw = m.exec_width < 16 && m.bits <= 12;
+    switch (m.bits) {
+#define EBX_PG_CASE(BB)                                                       \
+    case BB:                                                                  \
+        return hw ? launch_pgemm_b<BB, true>(tx, tc, a, grid, smem, dev, s)   \
+                  : launch_pgemm_b<BB, false>(tx, tc, a, grid, smem, dev, s);
+        EBX_PG_CASE(3) EBX_PG_CASE(4) EBX_PG_CASE(5) EBX_PG_CASE(6) EBX_PG_CASE(7) EBX_PG_CASE(8)
+        EBX_PG_CASE(9) EBX_PG_CASE(10) EBX_PG_CASE(11) EBX_PG_CASE(12)
+#undef EBX_PG_CASE
+#define EBX_PG_CASE(BB) \
+    case BB:            \
+        return launch_pgemm_b<BB, false>(tx, tc, a, grid, smem, dev, s);
+        EBX_PG_CASE(13) EBX_PG_CASE(14) EBX_PG_CASE(15) EBX_PG_CASE(16)
+#undef EBX_PG_CASE
+        default:
+            return cudaErrorInvalidValue;
+    }
+}
 
 cudaError_t read_gemm_status(int* status, bool clear, cudaStream_t s) {
     cudaError_t e = cudaMemcpyFromSymbolAsync(status, g_gemm_status, sizeof(int), 0,
@@ -853,7 +1263,9 @@ cudaError_t launch_dgemm(const Matrix& m, const uint16_t* x, int64_t M, const ui
     if (p.stages < 2) return cudaErrorInvalidConfiguration;
     if (p.S > 1 && (ws == nullptr || ws_bytes < dgemm_workspace_bytes(m, M))) return cudaErrorInvalidValue;
     CUtensorMap tx;
-    if (!make_map(&tx, x, int(M), m.cols, p.mp)) return cudaErrorInvalidValue;
+    CUtensorMap tc;
+    if (!make_map(&tx, x, int(M), m.cols, p.mp) || !make_code_map(&tc, m, kDgGroups))
+        return cudaErrorInvalidValue;
     DgArgs a{};
     a.tiles = m.tiles;
     a.scales = m.scales;
@@ -878,14 +1290,14 @@ cudaError_t launch_dgemm(const Matrix& m, const uint16_t* x, int64_t M, const ui
     switch (m.bits) {
 #define EBX_DG_CASE(BB)                                                                  \
     case BB:                                                                             \
-        return hw ? launch_dgemm_b<BB, true>(m, tx, a, grid, p.smem, dev, s)             \
-                  : launch_dgemm_b<BB, false>(m, tx, a, grid, p.smem, dev, s);
+        return hw ? launch_dgemm_b<BB, true>(m, tx, tc, a, grid, p.smem, dev, s)         \
+                  : launch_dgemm_b<BB, false>(m, tx, tc, a, grid, p.smem, dev, s);
         EBX_DG_CASE(3) EBX_DG_CASE(4) EBX_DG_CASE(5) EBX_DG_CASE(6) EBX_DG_CASE(7) EBX_DG_CASE(8)
         EBX_DG_CASE(9) EBX_DG_CASE(10) EBX_DG_CASE(11) EBX_DG_CASE(12)
 #undef EBX_DG_CASE
 #define EBX_DG_CASE(BB) \
     case BB:            \
-        return launch_dgemm_b<BB, false>(m, tx, a, grid, p.smem, dev, s);
+        return launch_dgemm_b<BB, false>(m, tx, tc, a, grid, p.smem, dev, s);
         EBX_DG_CASE(13) EBX_DG_CASE(14) EBX_DG_CASE(15) EBX_DG_CASE(16)
 #undef EBX_DG_CASE
         default:

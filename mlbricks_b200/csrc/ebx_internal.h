@@ -98,16 +98,21 @@ cudaError_t read_gemm_status(int* status, bool clear, cudaStream_t s);
 // workspace of dgemm_workspace_bytes() reduced in split order.
 constexpr int64_t kDgemmMinRows = 16;
 constexpr int64_t kDgemmMaxRows = 256;
-// dgemm_route: the shape rule alone (16 < M <= 128, or M <= 256 with K >= 8192), which
+// dgemm_route: the shape rule alone (16 < M <= 256), which
 // also decides ebx_linear_workspace_bytes; dgemm_supported adds the activation checks.
 inline bool dgemm_route(const Matrix& m, int64_t M) {
-    return M > kDgemmMinRows && M <= kDgemmMaxRows && (M <= 128 || m.kt >= 128) && (m.cols % 8) == 0;
+    return M > kDgemmMinRows && M <= kDgemmMaxRows && (m.cols % 8) == 0;
 }
 bool dgemm_supported(const Matrix& m, int64_t M, const void* x);
 uint64_t dgemm_workspace_bytes(const Matrix& m, int64_t M);
 cudaError_t launch_dgemm(const Matrix& m, const uint16_t* x, int64_t M, const uint16_t* bias,
                          uint16_t* y, float* y32, void* ws, uint64_t ws_bytes, cudaStream_t s);
 cudaError_t read_dgemm_status(int* status, bool clear, cudaStream_t s);
+// Prefill decode-GEMM (larger M): persistent tcgen05 GEMM whose weight operand is
+// decoded from the codes into shared memory per 64-k block; no workspace.
+bool pgemm_supported(const Matrix& m, const void* x);
+cudaError_t launch_pgemm(const Matrix& m, const uint16_t* x, int64_t M, const uint16_t* bias,
+                         uint16_t* y, float* y32, cudaStream_t s);
 
 // ebx_analyze.cu ------------------------------------------------------------
 cudaError_t launch_analyze(const float* w, int rows, int cols, const float* x, int samples,

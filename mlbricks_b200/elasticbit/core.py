@@ -338,8 +338,10 @@ class _FusedGroup:
     At decode sizes (at most 16 rows) the first member called with an input runs
     every member in ONE launch (ebx_linear_multi: each matrix keeps its own
     width, scales and semantics) and keeps the other members' outputs until they
-    are asked for with that same input object (same tensor, same version, same
-    stream).  Any other call runs on its own.  Used only while every member is on
+    are asked for with that same input object (same tensor, storage and version
+    -- inference tensors have no version counter, so an in-place change of one
+    between two members' calls is not seen -- on the same stream).  Any other
+    call runs on its own.  Used only while every member is on
     the native route for decode sizes, so the arithmetic is the one each member
     would run alone.  This replaces the reference's fused execution, which
     concatenates the groups' dequantised FP16 weights (stage2f.py:382-420).
@@ -363,8 +365,15 @@ class _FusedGroup:
         rows = x.numel() // max(1, x.shape[-1])
         return 0 < rows <= 16 and all(self._native_decode(layer) for layer in self.layers)
 
+    @staticmethod
+    def _version(x: torch.Tensor) -> int:
+        try:
+            return x._version
+        except RuntimeError:  # inference tensors carry no version counter
+            return -1
+
     def output(self, layer: "_ElasticLinear", x: torch.Tensor) -> torch.Tensor:
-        key = (x._version, torch.cuda.current_stream(x.device).cuda_stream)
+        key = (self._version(x), x.data_ptr(), torch.cuda.current_stream(x.device).cuda_stream)
         if self._x is not x or self._key != key or id(layer) not in self._outputs:
             natives = [getattr(m.matrix, "_native", m.matrix) for m in self.layers]
             biases = [m._bias_for(x) for m in self.layers]

@@ -239,13 +239,18 @@ def test_decode_gemm_full_semantics(lib, rows, cols, bits, M):
 
 
 @pytest.mark.parametrize("bits", [4, 8, 9, 10, 11, 12])
-@pytest.mark.parametrize("M", [24, 128])
+@pytest.mark.parametrize("M", [24, 128, 300, 1024])
 def test_decode_gemm_integer_semantics(lib, bits, M):
     rows, cols = 3000, 1024
     h, q, s = make(lib, rows, cols, bits, seed=bits + M)
     _ebx.check(lib.ebx_matrix_set_execution_width(h.h, 8 if bits <= 8 else 12))
     x = torch.randn((M, cols), device=dev()).half()
-    y, y32 = run_ws(lib, h, x, rows)
+    if M > 256:
+        # prefill sizes honour integer semantics on the workspace-free decode-GEMM route (the
+        # optional fp16 workspace route computes the reference's fp16(q * s) prefill)
+        y, y32 = run(lib, h, x, rows)
+    else:
+        y, y32 = run_ws(lib, h, x, rows)
     torch.cuda.synchronize()
     check(y, y32, (x.double() @ q.double().t()) * s.double())
 

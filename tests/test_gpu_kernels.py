@@ -320,20 +320,20 @@ def test_device_status_healthy_after_all_kernels(lib):
     assert st.value == 0
 
 
-# weight-tile widths chosen by the launcher's cost model: 64 for small grids (and the ragged
-# M = 2100 x N = 2600), 128 for M = 512 x N = 4096, 256 for M >= 1024 x N = 4096
+# ragged token counts and rows (last tiles partly past M and N), K not a multiple of 64
 @pytest.mark.parametrize("M,rows,cols", [(65, 96, 512), (128, 256, 64), (300, 1000, 520),
                                          (256, 1536, 384), (512, 4096, 4096), (200, 4096, 14336),
                                          (1024, 4096, 512), (2048, 4096, 256), (2100, 2600, 200)])
 def test_prefill_gemm(lib, M, rows, cols):
-    """M > 256: exact fp16 weight materialised into the workspace, tcgen05 GEMM;
-    16 < M <= 256: the decode-GEMM (codes decoded into tensor-core tiles)."""
+    """Larger M with the workspace ebx_linear_workspace_bytes offers: materialise +
+    tcgen05 GEMM; 16 < M <= 256: the decode-GEMM with the weights as the MMA's
+    128-row side."""
     bits = 10
     w = O.baseline_weights(rows, cols, seed=M + rows)
     s = O.row_scales(w, bits)
     q = O.quantize(w, s, bits)
     h = from_codes(lib, q, s, bits)
-    if M > 256:
+    if M > 256:  # optional workspace: the exact fp16 weight (materialise + GEMM route)
         assert lib.ebx_linear_workspace_bytes(h.h, M) >= rows * cols * 2
     x = O.normal((M, cols), seed=M).astype(np.float16)
     bias = O.normal((rows,), seed=5, scale=0.1).astype(np.float16)
@@ -345,14 +345,34 @@ def test_prefill_gemm(lib, M, rows, cols):
     assert np.array_equal(y32b, y32)  # deterministic
 
 
-def test_prefill_without_workspace_is_refused(lib):
-    q, s = random_codes(64, 128, 9, seed=2)
-    h = from_codes(lib, q, s, 9)
-    x = torch.zeros((300, 128), dtype=torch.float16, device=dev())
-    y = torch.empty((300, 64), dtype=torch.float16, device=dev())
-    st = lib.ebx_linear(h.h, x.data_ptr(), 300, None, y.data_ptr(), None, None, 0, stream())
-    assert st == _ebx.EBX_ERR_WORKSPACE
-    # decode-GEMM with K split over CTAs: the fp32 partials need the workspace too
+@pytest.mark.parametrize("M,rows,cols,bits", [(300, 1000, 520, 10), (1024, 4096, 512, 9),
+                                              (2100, 2600, 200, 12), (512, 4096, 4096, 11)])
+def test_prefill_without_workspace(lib, M, rows, cols, bits):
+    """Larger M and no workspace: the prefill decode-GEMM decodes the codes into the
+    tensor-core B tile per k-block (no memory beyond inputs and outputs)."""
+    w = O.baseline_weights(rows, cols, seed=M + bits)
+    s = O.row_scales(w, bits)
+    q = O.quantize(w, s, bits)
+    h = from_codes(lib, q, s, bits)
+    x = torch.from_numpy(O.normal((M, cols), seed=M).astype(np.float16)).to(dev())
+    bias = torch.from_numpy(O.normal((rows,), seed=5, scale=0.1).astype(np.float16)).to(dev())
+    xb = x.cpu().numpy().astype(np.float64)
+    bb = bias.cpu().numpy().astype(np.float64)
+    w16 = O.dequantize_codes(q, s).astype(np.float64)
+    refs = {16: xb @ w16.T + bb,  # fullPrecision: fp16(q * s) operands
+            12: (xb @ q.astype(np.float64).T) * s.astype(np.float64) + bb}  # integer codes
+    for width in (16, 12):
+        _ebx.check(lib.ebx_matrix_set_execution_width(h.h, width))
+        y = torch.empty((M, rows), dtype=torch.float16, device=dev())
+        y32 = torch.empty((M, rows), dtype=torch.float32, device=dev())
+        _ebx.check(lib.ebx_linear(h.h, x.data_ptr(), M, bias.data_ptr(), y.data_ptr(),
+                                  y32.data_ptr(), None, 0, stream()))
+        torch.cuda.synchronize()
+        assert_close_to_oracle(y.cpu().numpy(), y32.cpu().numpy(), refs[width])
+
+
+def test_split_k_without_workspace_is_refused(lib):
+    # decode-GEMM with K split over CTAs: the fp32 partials need the caller's workspace
     q, s = random_codes(512, 4096, 9, seed=3)
     h = from_codes(lib, q, s, 9)
     assert lib.ebx_linear_workspace_bytes(h.h, 100) > 0
