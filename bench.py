@@ -619,7 +619,9 @@ def _time_stack(layers, head, world: int, device, steps: int, coll) -> dict:
 def tp_parity(layers, head, bits_of, world: int, rank: int, device, coll) -> dict:
     """Sharded vs unsharded outputs of one layer of every kind (column QKV, row O,
     fused SwiGLU gate/up, row down, column lm_head and its greedy argmax) on this
-    rank's GPU, at M = 1, 16 (exchange route for row layers) and 64 (NCCL route).
+    rank's GPU, at M = 1, 16 and 64.
+    Row layers take the libebx exchange (fused decode at M <= 16, exchange all-reduce of
+    the fp32 partials at M = 64) when one is attached, NCCL otherwise.
     The unsharded matrices are rebuilt from the same seeds and run with the same
     integer-code semantics.  Bar: |y - ref| <= max(2e-3, one fp16 ulp of ref)
     elementwise and relative L2 <= 1e-3; every rank's result is reduced (max)."""
@@ -682,7 +684,7 @@ def tp_parity(layers, head, bits_of, world: int, rank: int, device, coll) -> dic
             "elements_over_tol": int(t[2]), "argmax_mismatch": int(t[3]),
             "ok": bool(t[1] <= 1e-3 and t[2] == 0 and t[3] == 0), "ranks": world,
             "M": [1, 16, 64],
-            "layers": "qkv (column), o (row; exchange at M <= 16, NCCL at 64), gate/up SwiGLU "
+            "layers": "qkv (column), o (row; libebx exchange, or NCCL without one), gate/up SwiGLU "
                       "(column, fused), down (row), lm_head (column) + distributed greedy argmax",
             "bar": "|y - ref| <= max(2e-3, fp16 ulp) elementwise, relative L2 <= 1e-3; "
                    "ref = the unsharded matrix on the same GPU"}
@@ -707,13 +709,14 @@ def run_tp_stack(args, world: int, rank: int, device) -> dict:
     coll = tp.Collectives.from_group() if world > 1 else None
     # decode batches <= 16: row-parallel layers all-reduce through the libebx exchange
     # (fp32 partials stored into every rank's region over NVLink); larger M: NCCL
-    exchange = (tp.Exchange.from_group(16, 4096)
+    exchange = (tp.Exchange.from_group(64, 4096)
                 if world > 1 and not getattr(args, "nccl_only", False) else None)
     layers, head, bits_of = build_stack(device, world, rank, coll, exchange)
     out = {"workload": "config5: 32 x (QKV 4096->6144 col, O 4096->4096 row, gate/up 4096->14336 "
                        "col, down 14336->4096 row) + lm_head 4096->128256 col, threshold 0.01; "
                        f"Megatron TP over {world} GPU(s); row-parallel all-reduce: "
-                       + ("libebx exchange (M<=16), NCCL fp32 (M>16)" if exchange else
+                       + ("libebx exchange (fused into the decode at M<=16, ebx_exchange_allreduce "
+                          "of the fp32 partials at M<=64), NCCL fp32 (prefill)" if exchange else
                           "NCCL fp32" if world > 1 else "none") +
                        "; gate/up interleaved per rank with SwiGLU fused into the decode epilogue (M<=16); "
                        "integer-code semantics pinned on every rank; greedy ids by a distributed argmax "
@@ -850,8 +853,11 @@ def _bolt_model(device):
     """BoltModel-shaped decoder (vocab 32000, dim 384, 12 query heads over one shared
     key/value head, 6 pre-norm layers, FFN 4x with GELU, RMSNorm, tied FP16 output
     head), N(0, 0.02) init, FP16.  Attention is plain multi-query scaled-dot-product
-    attention over a key/value cache; BOLT's own attention variants are not on the
-    compressed-linear path, every projection and FFN matrix is."""
+    attention over a key/value cache, gated per head and mixed with a gated value path;
+    the reference block's compressed projection shapes are all present (Q 384x384, K/V
+    32x384, the AVQ projection 768x384, the head gate 12x384 with bias, O, FFN up/down),
+    while BOLT's own attention machinery (AVQ codebooks, memory, retention) is not on
+    the compressed-linear path and is not reproduced."""
     import torch
     import torch.nn as nn
     import torch.nn.functional as F
@@ -867,6 +873,10 @@ def _bolt_model(device):
             self.q = nn.Linear(d, d, bias=False)
             self.k = nn.Linear(d, hd * c["kv_heads"], bias=False)
             self.v = nn.Linear(d, hd * c["kv_heads"], bias=False)
+            # the reference block's other compressed projections of the normalised input:
+            # a 2d-wide AVQ projection and a per-head output gate with bias
+            self.avq = nn.Linear(d, 2 * d, bias=False)
+            self.head_gate = nn.Linear(d, c["heads"], bias=True)
             self.o = nn.Linear(d, d, bias=False)
             self.n2 = nn.RMSNorm(d, eps=1e-6)
             self.up = nn.Linear(d, c["ffn_mult"] * d, bias=False)
@@ -879,6 +889,8 @@ def _bolt_model(device):
             q = self.q(a).view(B, T, c["heads"], hd).transpose(1, 2)
             k = self.k(a).view(B, T, 1, hd).transpose(1, 2)
             v = self.v(a).view(B, T, 1, hd).transpose(1, 2)
+            u, ug = self.avq(a).chunk(2, dim=-1)                  # value path and its gate
+            gate = torch.sigmoid(self.head_gate(a)).view(B, T, c["heads"], 1)
             kc.index_copy_(2, pos, k)
             vc.index_copy_(2, pos, v)
             if T > 1:  # prefill from position 0: causal attention over these tokens
@@ -888,7 +900,8 @@ def _bolt_model(device):
                 s = (q @ kc.transpose(-1, -2)) * (hd ** -0.5)
                 mask = torch.arange(L, device=h.device) > pos
                 att = torch.softmax(s.float().masked_fill(mask, float("-inf")), -1).to(vc.dtype) @ vc
-            h = h + self.o(att.transpose(1, 2).reshape(B, T, -1))
+            att = (att.transpose(1, 2) * gate).reshape(B, T, -1) + u * torch.sigmoid(ug)
+            h = h + self.o(att)
             return h + self.down(F.gelu(self.up(self.n2(h))))
 
     class Decoder(nn.Module):
@@ -1016,7 +1029,9 @@ def run_bolt_decoder(device) -> dict:
     res["workload"] = ("config4: BoltModel-shaped decoder (vocab 32000, dim 384, 12 q heads / 1 kv "
                        "head, 6 layers, FFN 4x, tied FP16 head), N(0,0.02) init; batch 8, 512-token "
                        "prefill of uniform random ids, 128 greedy steps (one CUDA graph per step); "
-                       "plain multi-query attention")
+                       "plain multi-query attention with the reference block's AVQ projection "
+                       "(768x384) and per-head output gate (12x384 + bias); Q/K/V/AVQ/gate run as "
+                       "one fused decode launch per block")
     del dense, comp
     torch.cuda.empty_cache()
     return res

@@ -221,7 +221,7 @@ EBX_API ebx_status ebx_linear_swiglu(const ebx_matrix* m, const void* x, int64_t
  * W_i^T (+ biases[i]), i < count.  Replaces the reference's fused multi-matrix
  * execution, which concatenates the dequantised FP16 weights of such a group
  * into one matrix for a single GEMM (mlbricks/elasticbit/stage2f.py:382-420);
- * here the codes stay at their own widths.  1 <= count <= 4, 0 <= M <= 16,
+ * here the codes stay at their own widths.  1 <= count <= 8, 0 <= M <= 16,
  * every matrix on one device with the same cols; biases, y32s (and their
  * entries) may be NULL.  EBX_ERR_UNSUPPORTED (nothing launched) unless every
  * storage width is 8..12, cols % 64 == 0 and x is 16-byte aligned: run such
@@ -262,8 +262,9 @@ EBX_API ebx_status ebx_linear_multi(const ebx_matrix* const* mats, int32_t count
 
 typedef struct ebx_exchange ebx_exchange;
 
-/* Allocate this rank's region on `device`; 1 <= world <= 8, 1 <= max_m <= 16.
- * handle_out receives EBX_EXCHANGE_HANDLE_BYTES bytes. */
+/* Allocate this rank's region on `device`; 1 <= world <= 8, 1 <= max_m <= 256
+ * (ebx_linear_allreduce itself takes M <= 16).  handle_out receives
+ * EBX_EXCHANGE_HANDLE_BYTES bytes. */
 EBX_API ebx_status ebx_exchange_create(int32_t world, int32_t rank, int32_t device, int64_t max_m,
                                        int64_t max_n, void* handle_out, ebx_exchange** out);
 /* Map the regions of all ranks: `handles` = world blobs in rank order. */
@@ -276,6 +277,18 @@ EBX_API ebx_status ebx_exchange_destroy(ebx_exchange* ex);
 EBX_API ebx_status ebx_linear_allreduce(const ebx_matrix* m, const void* x, int64_t M,
                                         const void* bias, void* y, float* y32, ebx_exchange* ex,
                                         void* stream);
+
+/* y[M, N] (fp16) = fp16( sum over ranks of partial_r + bias ) for an fp32 partial
+ * [M, N] this rank already holds -- a row-parallel shard's fp32 output from
+ * ebx_linear (y32) at batch sizes above ebx_linear_allreduce's 16 rows -- over the
+ * same exchange: one cooperative launch stores every element into every rank's
+ * region and sums all ranks' words in rank order (bit-identical on every rank),
+ * replacing an NCCL all-reduce of the partials.  M <= max_m, N <= max_n; bias (fp16,
+ * may be NULL), y32 (fp32 copy before rounding, may be NULL).  The same call-order
+ * rules as ebx_linear_allreduce; no reference counterpart. */
+EBX_API ebx_status ebx_exchange_allreduce(ebx_exchange* ex, const float* partial, int64_t M,
+                                          int64_t N, const void* bias, void* y, float* y32,
+                                          void* stream);
 
 #ifdef __cplusplus
 }

@@ -444,15 +444,15 @@ ebx_status ebx_linear_multi(const ebx_matrix* const* mats, int32_t count, const 
         set_error("null argument");
         return EBX_ERR_INVALID;
     }
-    if (count > 4) {
-        set_error("ebx_linear_multi: at most 4 matrices per launch");
+    if (count > 8) {
+        set_error("ebx_linear_multi: at most 8 matrices per launch");
         return EBX_ERR_INVALID;
     }
     if (M < 0 || M > 16) {
         set_error("ebx_linear_multi: need 0 <= M <= 16 (decode batches)");
         return EBX_ERR_INVALID;
     }
-    const ebx::Matrix* ms[4];
+    const ebx::Matrix* ms[8];
     for (int i = 0; i < count; ++i) {
         if (!mats[i] || !ys[i]) {
             set_error("null argument");
@@ -509,8 +509,8 @@ ebx_status ebx_exchange_create(int32_t world, int32_t rank, int32_t device, int6
         set_error("exchange: need 1 <= world <= 8 and 0 <= rank < world");
         return EBX_ERR_INVALID;
     }
-    if (max_m < 1 || max_m > 16 || max_n < 1 || max_n > (int64_t(1) << 24)) {
-        set_error("exchange: need 1 <= max_m <= 16 and 1 <= max_n <= 2^24");
+    if (max_m < 1 || max_m > 256 || max_n < 1 || max_n > (int64_t(1) << 24)) {
+        set_error("exchange: need 1 <= max_m <= 256 and 1 <= max_n <= 2^24");
         return EBX_ERR_INVALID;
     }
     DeviceGuard g(device);
@@ -632,8 +632,9 @@ ebx_status ebx_linear_allreduce(const ebx_matrix* h, const void* x, int64_t M, c
         set_error("exchange not connected (ebx_exchange_connect)");
         return EBX_ERR_INVALID;
     }
-    if (M < 0 || M > ex->max_m || int64_t(h->m.rows) > ex->max_n) {
-        set_error("ebx_linear_allreduce: need 0 <= M <= max_m and rows <= max_n of the exchange");
+    if (M < 0 || M > ex->max_m || M > 16 || int64_t(h->m.rows) > ex->max_n) {
+        set_error("ebx_linear_allreduce: need 0 <= M <= min(16, max_m) and rows <= max_n of the "
+                  "exchange (larger M: ebx_linear's fp32 output, then ebx_exchange_allreduce)");
         return EBX_ERR_INVALID;
     }
     if (h->m.device != ex->device) {
@@ -651,6 +652,28 @@ ebx_status ebx_linear_allreduce(const ebx_matrix* h, const void* x, int64_t M, c
     if (!xa.fused)
         EBX_CUDA(ebx::launch_xchg_finish(xa, int(M), h->m.rows, static_cast<const uint16_t*>(bias),
                                          static_cast<uint16_t*>(y), y32, s));
+    return EBX_OK;
+}
+
+ebx_status ebx_exchange_allreduce(ebx_exchange* ex, const float* partial, int64_t M, int64_t N,
+                                  const void* bias, void* y, float* y32, void* stream) {
+    if (!ex || (M > 0 && N > 0 && (!partial || !y))) {
+        set_error("null argument");
+        return EBX_ERR_INVALID;
+    }
+    if (!ex->connected) {
+        set_error("exchange not connected (ebx_exchange_connect)");
+        return EBX_ERR_INVALID;
+    }
+    if (M < 0 || N < 0 || M > ex->max_m || N > ex->max_n) {
+        set_error("ebx_exchange_allreduce: need 0 <= M <= max_m and 0 <= N <= max_n");
+        return EBX_ERR_INVALID;
+    }
+    if (M == 0 || N == 0) return EBX_OK;
+    DeviceGuard g(ex->device);
+    EBX_CUDA(ebx::launch_xchg_allreduce(ex->xa, partial, int(M), int(N),
+                                        static_cast<const uint16_t*>(bias), static_cast<uint16_t*>(y),
+                                        y32, static_cast<cudaStream_t>(stream)));
     return EBX_OK;
 }
 

@@ -45,7 +45,62 @@ __global__ void __launch_bounds__(kFinishThreads) xchg_finish_kernel(XchgArgs xa
     xchg_advance(xa, e);
 }
 
+// One-shot all-reduce of an fp32 partial [M, N] that this rank already holds (a
+// row-parallel shard's y32 from the decode-GEMM): every CTA first stores all of its
+// elements into every rank's region, then gathers them; the launch is cooperative,
+// so every CTA of every rank gets to store before any of them can be waited on.
+__global__ void __launch_bounds__(kFinishThreads) xchg_allreduce_kernel(XchgArgs xa, const float* part,
+                                                                        int M, int N,
+                                                                        const uint16_t* bias,
+                                                                        uint16_t* y, float* y32) {
+    const uint32_t e = xchg_epoch(xa) + 1u;
+    const size_t total = size_t(M) * size_t(N);
+    const size_t step = size_t(gridDim.x) * kFinishThreads;
+    const size_t first = size_t(blockIdx.x) * kFinishThreads + threadIdx.x;
+    for (size_t i = first; i < total; i += step)
+        xchg_push(xa, e, M, N, int(i / size_t(N)), int(i % size_t(N)), part[i]);
+    bool ok = true;
+    for (size_t i = first; i < total; i += step) {
+        float v;
+        if (!xchg_gather(xa, e, M, N, int(i / size_t(N)), int(i % size_t(N)), v)) {
+            ok = false;
+            break;
+        }
+        const int row = int(i % size_t(N));
+        if (bias) v += __half2float(__ushort_as_half(bias[row]));
+        y[i] = __half_as_ushort(__float2half_rn(v));
+        if (y32) y32[i] = v;
+    }
+    if (!ok) atomicExch(&g_xchg_status, kXchgTimeout);
+    xchg_advance(xa, e);
+}
+
 }  // namespace
+
+cudaError_t launch_xchg_allreduce(const XchgArgs& xa, const float* part, int M, int N,
+                                  const uint16_t* bias, uint16_t* y, float* y32, cudaStream_t s) {
+    int dev = 0, sms = 0, per_sm = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess)
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, xchg_allreduce_kernel, kFinishThreads, 0);
+    if (e != cudaSuccess) return e;
+    const size_t total = size_t(M) * size_t(N);
+    size_t blocks = (total + kFinishThreads - 1) / kFinishThreads;
+    const size_t cap = size_t(sms) * size_t(per_sm < 4 ? per_sm : 4);
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(blocks));
+    cfg.blockDim = dim3(kFinishThreads);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, xchg_allreduce_kernel, xa, part, M, N, bias, y, y32);
+}
 
 cudaError_t launch_xchg_finish(const XchgArgs& xa, int M, int N, const uint16_t* bias,
                                uint16_t* y, float* y32, cudaStream_t s) {

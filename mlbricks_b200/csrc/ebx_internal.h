@@ -85,6 +85,10 @@ cudaError_t read_device_status(int* status, bool clear, cudaStream_t s);
 cudaError_t launch_xchg_finish(const XchgArgs& xa, int M, int N, const uint16_t* bias,
                                uint16_t* y, float* y32, cudaStream_t s);
 cudaError_t read_xchg_status(int* status, bool clear, cudaStream_t s);
+// The same exchange for an fp32 partial the caller already holds (M up to the exchange's
+// max_m): push to every rank, gather in rank order, bias, one rounding, advance the epoch.
+cudaError_t launch_xchg_allreduce(const XchgArgs& xa, const float* part, int M, int N,
+                                  const uint16_t* bias, uint16_t* y, float* y32, cudaStream_t s);
 
 // ebx_gemm.cu ---------------------------------------------------------------
 // Rows above which ebx_linear takes the materialise + tcgen05 GEMM route.

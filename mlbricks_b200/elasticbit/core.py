@@ -607,7 +607,7 @@ class _RowRecorder:
             self._rows.pop(n, None)
 
     def siblings(self, names: Sequence[str]) -> list[list[str]]:
-        """Groups (2..4 names, in `names` order) whose first call received the very
+        """Groups (2..8 names, in `names` order) whose first call received the very
         same input tensor object."""
         by_input: dict[int, list[str]] = {}
         for n in names:
@@ -615,7 +615,7 @@ class _RowRecorder:
             if x is not None:
                 by_input.setdefault(id(x), []).append(n)
         self._first.clear()
-        return [g for g in by_input.values() if 2 <= len(g) <= 4]
+        return [g for g in by_input.values() if 2 <= len(g) <= 8]
 
 
 @dataclass

@@ -21,8 +21,9 @@ CPU and a stand-in compute function.
 For decode-sized inputs (M <= 16) a row-parallel layer can skip the collective
 altogether: with an :class:`Exchange` attached, one libebx call
 (``ebx_linear_allreduce``) runs the shard's decode kernel, which stores its fp32
-partials straight into every rank's exchange region over NVLink, and a finish
-kernel that waits for all ranks' epoch flags and sums the partials in rank order.
+partials straight into every rank's exchange region over NVLink and sums all ranks'
+partials in rank order.  Up to the exchange's ``max_m`` rows the shard's fp32 output
+is summed the same way by ``ebx_exchange_allreduce`` instead of an NCCL all-reduce.
 """
 from __future__ import annotations
 
@@ -132,6 +133,24 @@ class Exchange:
         dist.barrier(group)  # every rank has mapped every region before the first use
         return ex
 
+    def allreduce(self, partial: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+        """fp16(sum over ranks of `partial` + bias) for an fp32 [M, N] partial this rank
+        holds (ebx_exchange_allreduce; M <= max_m, N <= max_n): one launch over NVLink
+        peer memory instead of an NCCL all-reduce, summed in rank order on every rank."""
+        from .. import _ebx
+
+        part = partial.contiguous()
+        M, N = (int(part.shape[0]), int(part.shape[1])) if part.dim() == 2 else (1, int(part.numel()))
+        y = torch.empty(part.shape, dtype=torch.float16, device=part.device)
+        b = None
+        if bias is not None:
+            b = bias.detach().to(device=part.device, dtype=torch.float16).contiguous()
+        _ebx.check(self._lib.ebx_exchange_allreduce(self.handle, part.data_ptr(), M, N,
+                                                    None if b is None else b.data_ptr(),
+                                                    y.data_ptr(), None,
+                                                    _ebx.stream_ptr(device=part.device.index)))
+        return y
+
     def close(self) -> None:
         h = getattr(self, "handle", None)
         if h is not None and h.value:
@@ -204,10 +223,15 @@ class ShardedLinear(torch.nn.Module):
         lo, hi = self.bounds
         xs = x.contiguous() if self.input_is_local else x[..., lo:hi].contiguous()
         ex = self.exchange
-        if ex is not None and self._local is None and xs.numel() // max(1, xs.shape[-1]) <= ex.max_m:
+        rows = xs.numel() // max(1, xs.shape[-1])
+        if ex is not None and self._local is None and rows <= min(16, ex.max_m):
             native = getattr(self.matrix, "_native", self.matrix)
             return native.linear_allreduce(xs, ex, bias=self.bias)
         part = self._compute(xs, True, None)
+        if ex is not None and self._local is None and rows <= ex.max_m and \
+                self.out_features <= ex.max_n:
+            y = ex.allreduce(part.reshape(rows, self.out_features), self.bias)
+            return y.view(*part.shape)
         if self.collectives is not None:
             self.collectives.allreduce(part)
         if self.bias is not None:

@@ -69,7 +69,7 @@ def test_exchange_argument_errors_without_gpu():
     assert lib.ebx_exchange_create(9, 0, 0, 1, 16, blob, ctypes.byref(h)) == _ebx.EBX_ERR_INVALID
     assert "world" in _ebx.last_error()
     assert lib.ebx_exchange_create(2, 2, 0, 1, 16, blob, ctypes.byref(h)) == _ebx.EBX_ERR_INVALID
-    assert lib.ebx_exchange_create(2, 0, 0, 17, 16, blob, ctypes.byref(h)) == _ebx.EBX_ERR_INVALID
+    assert lib.ebx_exchange_create(2, 0, 0, 257, 16, blob, ctypes.byref(h)) == _ebx.EBX_ERR_INVALID
     assert "max_m" in _ebx.last_error()
     assert lib.ebx_exchange_create(2, 0, 0, 1, 16, None, ctypes.byref(h)) == _ebx.EBX_ERR_INVALID
     assert lib.ebx_exchange_connect(None, blob) == _ebx.EBX_ERR_INVALID

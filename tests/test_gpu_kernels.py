@@ -270,10 +270,13 @@ def test_device_quantizer_bit_exact(lib, bits):
 
 @pytest.mark.parametrize("bits", [2, 3, 5, 8])
 @pytest.mark.parametrize("xdt", [torch.float16, torch.bfloat16, torch.float32])
-def test_elastic_linear_packed_op(lib, bits, xdt):
+@pytest.mark.parametrize("rows,group", [(3, 50), (70, 30)])
+def test_elastic_linear_packed_op(lib, bits, xdt, rows, group):
+    """Rows beyond one 8-row chunk and one 64-row block, and scale groups that straddle
+    output features (group 30 over 100 inputs), against the oracle's scalar loop."""
     import mlbricks_b200.native as native
 
-    rows, inf, outf, group = 3, 100, 24, 50
+    inf, outf = 100, 24
     rng = np.random.default_rng(bits)
     uq = rng.integers(0, 1 << bits, size=outf * inf)
     packed = np.zeros((outf * inf * bits + 7) // 8 + 1, np.uint8)

@@ -61,7 +61,7 @@ def _worker(rank, world, port, q_out):
         q, s, bits, bias, xs = _case()
         bias_t = torch.from_numpy(bias).cuda()
         coll = tp.Collectives.from_group()
-        ex = tp.Exchange.from_group(16, 4096)
+        ex = tp.Exchange.from_group(128, 4096)  # M <= 16: fused decode; 16 < M <= 128: allreduce
         res = {}
         lin = {mode: tp.build_sharded(q, s, bits, mode, world, rank, bias=bias_t,
                                       collectives=coll, gather=True) for mode in tp.MODES}
@@ -131,7 +131,7 @@ def test_tensor_parallel_matches_single_gpu(cuda_ok):
                 assert np.all(np.abs(y - ref[M]) <= tol), (M, mode, rank)
                 if mode == "column":  # every rank gathers the same shards
                     assert np.array_equal(y, results[0][(M, mode)])
-            if M <= 16:
+            if M <= 128:  # fused decode exchange (M <= 16) or ebx_exchange_allreduce
                 y0 = res[(M, "exchange", 0)]
                 assert np.all(np.abs(y0 - ref[M]) <= tol), (M, "exchange", rank)
                 for rep in (1, 2):
