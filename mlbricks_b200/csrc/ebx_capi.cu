@@ -119,6 +119,7 @@ ebx_status alloc_matrix(int rows, int cols, int bits, int device, ebx_matrix** o
         e = cudaMalloc(reinterpret_cast<void**>(&m.scales), sizeof(float) * size_t(rows));
     if (e != cudaSuccess) {
         if (m.tiles) cudaFree(m.tiles);
+        if (m.scales) cudaFree(m.scales);
         delete h;
         return cuda_fail(e, "cudaMalloc(matrix buffers)");
     }

@@ -360,36 +360,101 @@ __device__ __forceinline__ void pdl_trigger() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// Consumer warp of the plane-layout decode (b = 8..12, one row group per CTA):
-// per ring round it takes TPW consecutive supertiles of the round's 8 * TPW,
-// decodes each lane's 32 codes to exact fp16 q pairs with byte permutes
-// (plane_q16_all) and issues mma.m16n8k16 against the staged activations.
+// One ring round of a plane-decode consumer warp: TPW consecutive supertiles of the
+// round (those with index < rem), their codes decoded to exact fp16 q pairs with byte
+// permutes (plane_q16_all) and multiplied by mma.m16n8k16 against the staged
+// activations into acc.  The warp releases the stage (empty barrier) once every
+// shared-memory load of it has been issued.
 //   HW:   integer codes as operands, row scale applied after accumulation
 //         (the epilogue multiplies); fp16 holds every |q| <= 2047 exactly.
-//   !HW:  fp16_rn(fp32_rn(q * s)) operands (W16A16 semantics), from the same q.
-// Leaves the fp32 fragment sums of this warp in red[] for the CTA reduction.
+//   !HW:  fp16_rn(fp32_rn(q * s)) operands (W16A16 semantics), from the same q;
+//         s2 = (s, s) of the lane's two rows.
+template <int B, bool HW, int NT, int TPW, class S>
+__device__ __forceinline__ void plane_round(const uint8_t* smem, int so, int rem, int w16, int w8,
+                                            int w4, const int (&xa)[NT], const PlaneConsts& pk,
+                                            const uint64_t (&s2)[2], float (&acc)[NT][4],
+                                            uint32_t empty_bar, int lane) {
+#pragma unroll
+    for (int j = 0; j < TPW; ++j) {
+        const bool have = rem > j;
+        uint32_t w[B];
+        uint32_t xb[NT][8];
+        if (have) {
+            const int T0 = so + j * S::kTileBytes;
+#pragma unroll
+            for (int q = 0; q < B / 4; ++q) {
+                const uint4 v = *reinterpret_cast<const uint4*>(smem + w16 + T0 + q * 512);
+                w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
+            }
+            if constexpr ((B & 2) != 0) {
+                const uint2 v = *reinterpret_cast<const uint2*>(smem + w8 + T0 + (B / 4) * 512);
+                w[4 * (B / 4)] = v.x;
+                w[4 * (B / 4) + 1] = v.y;
+            }
+            if constexpr ((B & 1) != 0)
+                w[B - 1] = *reinterpret_cast<const uint32_t*>(smem + w4 + T0 + (B / 4) * 512 +
+                                                              ((B & 2) ? 256 : 0));
+#pragma unroll
+            for (int nb = 0; nb < NT; ++nb)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(smem + xa[nb] + so +
+                                                                    j * kKTile * 2 + 16 * h);
+                    xb[nb][4 * h] = v.x; xb[nb][4 * h + 1] = v.y;
+                    xb[nb][4 * h + 2] = v.z; xb[nb][4 * h + 3] = v.w;
+                }
+        }
+        if (j == TPW - 1) {  // every load of this stage has been issued
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty_bar);
+        }
+        if (!have) continue;
+        uint32_t af[16];
+        plane_q16_all<B>(w, pk, af);
+        if constexpr (!HW) {
+#pragma unroll
+            for (int p = 0; p < 16; ++p) af[p] = q16_to_w16(af[p], s2[p & 1]);
+        }
+#pragma unroll
+        for (int s4 = 0; s4 < 4; ++s4) {
+            const uint32_t f[4] = {af[4 * s4], af[4 * s4 + 1], af[4 * s4 + 2], af[4 * s4 + 3]};
+#pragma unroll
+            for (int nb = 0; nb < NT; ++nb)
+                mma_16816(acc[nb], f, xb[nb][(s4 >> 1) * 4 + (s4 & 1) * 2],
+                          xb[nb][(s4 >> 1) * 4 + (s4 & 1) * 2 + 1]);
+        }
+    }
+}
+
+// (s, s) of the two rows lane `lane` holds in row group g (zero past N); only the
+// fullPrecision (!HW) decode multiplies by them.
+__device__ __forceinline__ void plane_row_scales(const DecodeArgs& a, int g, int lane,
+                                                 uint64_t (&s2)[2]) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int row = g * kRowGroup + (lane >> 2) + 8 * h;
+        const float sv = (g < a.groups && row < a.N) ? a.scales[row] : 0.0f;
+        s2[h] = pack2f(sv, sv);
+    }
+}
+
+// Consumer warp of the plane-layout decode (b = 8..12): per ring round it takes TPW
+// consecutive supertiles of the round's 8 * TPW (plane_round).  Leaves the fp32
+// fragment sums of this warp in red[] for the CTA reduction.
 template <int B, bool HW, int NT, int TPW, int RG, class S>
 __device__ __forceinline__ void plane_consume(const DecodeArgs& a, uint8_t* smem, uint32_t full0,
-                                              uint32_t empty0, int tile0, int rounds, int mrows,
-                                              int warp, int lane, float* red, int cta) {
+                                              uint32_t empty0, int rounds, int mrows, int warp,
+                                              int lane, float* red, int cta) {
     const int rgl = warp / kWarps;  // local row group (RG > 1: the groups share each activation stage)
     const int wt = warp % kWarps;   // tile slot within the round
     const int g = cta * RG + rgl;
     const bool grp_ok = g < a.groups;
     const int r0 = lane >> 2;
     const int c = lane & 3;
-    const int row_lo = g * kRowGroup + r0;
     PlaneConsts pk;
     pk.init(a.magic_plane);
     uint64_t s2[2] = {0, 0};
-    if constexpr (!HW) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int row = row_lo + 8 * h;
-            const float sv = (grp_ok && row < a.N) ? a.scales[row] : 0.0f;
-            s2[h] = pack2f(sv, sv);
-        }
-    }
+    if constexpr (!HW) plane_row_scales(a, g, lane, s2);
     float acc[NT][4];
 #pragma unroll
     for (int nb = 0; nb < NT; ++nb)
@@ -405,8 +470,7 @@ __device__ __forceinline__ void plane_consume(const DecodeArgs& a, uint8_t* smem
         xa[nb] = RG * S::kWBytes + (tok < mrows ? tok : mrows) * S::kXStride + wt * TPW * kKTile * 2 +
                  32 * c;
     }
-    // tiles of this warp's slot still ahead (this CTA's K part starts at tile0)
-    int rem = grp_ok ? a.kt - tile0 - wt * TPW : 0;
+    int rem = grp_ok ? a.kt - wt * TPW : 0;  // tiles of this warp's slot still ahead
     int so = 0, st = 0;
     uint32_t ph = 0;
     for (int r = 0; r < rounds; ++r) {
@@ -414,56 +478,8 @@ __device__ __forceinline__ void plane_consume(const DecodeArgs& a, uint8_t* smem
             if (lane == 0) atomicExch(&g_device_status, kDeviceTimeout);
             break;
         }
-#pragma unroll
-        for (int j = 0; j < TPW; ++j) {
-            const bool have = rem > j;
-            uint32_t w[B];
-            uint32_t xb[NT][8];
-            if (have) {
-                const int T0 = so + j * S::kTileBytes;
-#pragma unroll
-                for (int q = 0; q < B / 4; ++q) {
-                    const uint4 v = *reinterpret_cast<const uint4*>(smem + w16 + T0 + q * 512);
-                    w[4 * q] = v.x; w[4 * q + 1] = v.y; w[4 * q + 2] = v.z; w[4 * q + 3] = v.w;
-                }
-                if constexpr ((B & 2) != 0) {
-                    const uint2 v = *reinterpret_cast<const uint2*>(smem + w8 + T0 + (B / 4) * 512);
-                    w[4 * (B / 4)] = v.x;
-                    w[4 * (B / 4) + 1] = v.y;
-                }
-                if constexpr ((B & 1) != 0)
-                    w[B - 1] = *reinterpret_cast<const uint32_t*>(smem + w4 + T0 + (B / 4) * 512 +
-                                                                  ((B & 2) ? 256 : 0));
-#pragma unroll
-                for (int nb = 0; nb < NT; ++nb)
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const uint4 v = *reinterpret_cast<const uint4*>(smem + xa[nb] + so +
-                                                                        j * kKTile * 2 + 16 * h);
-                        xb[nb][4 * h] = v.x; xb[nb][4 * h + 1] = v.y;
-                        xb[nb][4 * h + 2] = v.z; xb[nb][4 * h + 3] = v.w;
-                    }
-            }
-            if (j == TPW - 1) {  // every load of this stage has been issued
-                __syncwarp();
-                if (lane == 0) mbar_arrive(empty0 + 8u * uint32_t(st));
-            }
-            if (!have) continue;
-            uint32_t af[16];
-            plane_q16_all<B>(w, pk, af);
-            if constexpr (!HW) {
-#pragma unroll
-                for (int p = 0; p < 16; ++p) af[p] = q16_to_w16(af[p], s2[p & 1]);
-            }
-#pragma unroll
-            for (int s4 = 0; s4 < 4; ++s4) {
-                const uint32_t f[4] = {af[4 * s4], af[4 * s4 + 1], af[4 * s4 + 2], af[4 * s4 + 3]};
-#pragma unroll
-                for (int nb = 0; nb < NT; ++nb)
-                    mma_16816(acc[nb], f, xb[nb][(s4 >> 1) * 4 + (s4 & 1) * 2],
-                              xb[nb][(s4 >> 1) * 4 + (s4 & 1) * 2 + 1]);
-            }
-        }
+        plane_round<B, HW, NT, TPW, S>(smem, so, rem, w16, w8, w4, xa, pk, s2, acc,
+                                       empty0 + 8u * uint32_t(st), lane);
         rem -= S::kRound;
         so += a.stage_bytes;
         if (++st == a.stages) {
@@ -485,13 +501,8 @@ __device__ __forceinline__ void plane_consume(const DecodeArgs& a, uint8_t* smem
 // written by the copy engine, so the fragment loads need no predicates.
 // The pipe decode of CTA `cta` of a launch over one matrix (decode_pipe_kernel: cta =
 // blockIdx.x; decode_multi_kernel: the CTA's index within its matrix's row groups).
-// KS > 1: the launch is a cluster of KS CTAs per row-group CTA, CTA `kpart` of the
-// cluster streams the kpart-th of KS equal runs of rounds, and parts 1..KS-1 store
-// their fp32 sums into part 0's shared memory (distributed shared memory) for the
-// epilogue, which adds them in part order (deterministic).
-template <int B, bool HW, int NT, bool DIRECT, int RG, int TPW, int KS = 1>
-__device__ __forceinline__ void decode_pipe_body(const DecodeArgs& a, const int cta,
-                                                 const int kpart = 0) {
+template <int B, bool HW, int NT, bool DIRECT, int RG, int TPW>
+__device__ __forceinline__ void decode_pipe_body(const DecodeArgs& a, const int cta) {
     using S = PipeStage<B, NT, RG, TPW>;
     constexpr int kConsumers = kWarps * RG;
     // plane layout (b = 9..12), and b = 8's byte codes under integer semantics
@@ -504,9 +515,7 @@ __device__ __forceinline__ void decode_pipe_body(const DecodeArgs& a, const int 
     float* red = reinterpret_cast<float*>(empty + kMaxStages);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int all_rounds = (a.kt + S::kRound - 1) / S::kRound;
-    const int r_begin = all_rounds * kpart / KS;  // this CTA's run of rounds
-    const int rounds = all_rounds * (kpart + 1) / KS - r_begin;
+    const int rounds = (a.kt + S::kRound - 1) / S::kRound;
     const int mrows = a.M < NT * 8 ? a.M : NT * 8;
     const uint32_t xe = a.xa.world ? xchg_epoch(a.xa) + 1u : 0u;  // epoch this call publishes
 
@@ -516,15 +525,12 @@ __device__ __forceinline__ void decode_pipe_body(const DecodeArgs& a, const int 
             mbar_init(smem_u32(&empty[i]), kConsumers);
         }
     }
-    // every CTA of the cluster has started before any touches another's shared
-    // memory (the matching wait precedes the epilogue's remote stores)
-    if constexpr (KS > 1) cluster_arrive_relaxed();
     // zero row (index mrows) of every stage, never written by the copy engine:
     // lanes whose token is >= M read it
     for (int i = threadIdx.x; i < D * (S::kXStride / 16); i += blockDim.x)
-            *reinterpret_cast<uint4*>(smem + (i / (S::kXStride / 16)) * SB + RG * S::kWBytes +
-                                      mrows * S::kXStride + (i % (S::kXStride / 16)) * 16) =
-                make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(smem + (i / (S::kXStride / 16)) * SB + RG * S::kWBytes +
+                                  mrows * S::kXStride + (i % (S::kXStride / 16)) * 16) =
+            make_uint4(0, 0, 0, 0);
     fence_proxy_async_smem();
     __syncthreads();
 
@@ -562,14 +568,13 @@ __device__ __forceinline__ void decode_pipe_body(const DecodeArgs& a, const int 
                          uint32_t(ntile * kKTile * 2), smem_u32(&full[st]));
         };
         const int pre = rounds < D ? rounds : D;
-        for (int i = 0; i < pre; ++i) weights(r_begin + i, i);
+        for (int r = 0; r < pre; ++r) weights(r, r);
         pdl_wait();
         __syncwarp();
-        for (int i = 0; i < pre; ++i) acts(r_begin + i, i);
-        for (int i = pre; i < rounds; ++i) {
-            const int r = r_begin + i;
-            const int st = i % D;
-            const uint32_t ph = uint32_t(i / D) & 1u;
+        for (int r = 0; r < pre; ++r) acts(r, r);
+        for (int r = pre; r < rounds; ++r) {
+            const int st = r % D;
+            const uint32_t ph = uint32_t(r / D) & 1u;
             if (!bounded_wait(smem_u32(&empty[st]), ph ^ 1u)) {
                 if (lane == 0) atomicExch(&g_device_status, kDeviceTimeout);
                 break;
@@ -583,8 +588,7 @@ __device__ __forceinline__ void decode_pipe_body(const DecodeArgs& a, const int 
         // ---------------- consumer warps ----------------
       if constexpr (kPlane) {
         plane_consume<B, HW, NT, TPW, RG, S>(a, smem, smem_u32(&full[0]), smem_u32(&empty[0]),
-                                             r_begin * S::kRound, rounds, mrows, warp, lane, red,
-                                             cta);
+                                             rounds, mrows, warp, lane, red, cta);
         if (!a.pdl_early) pdl_trigger();
       } else {
         const int rgl = warp / kWarps;   // local row group
@@ -647,7 +651,7 @@ __device__ __forceinline__ void decode_pipe_body(const DecodeArgs& a, const int 
         }
         const uint32_t full0 = smem_u32(&full[0]), empty0 = smem_u32(&empty[0]);
         // tiles of this warp's slot still ahead of the current round
-        int rem = grp_ok ? a.kt - r_begin * S::kRound - wt * TPW : 0;
+        int rem = grp_ok ? a.kt - wt * TPW : 0;
         int so = 0;
         int st = 0;
         uint32_t ph = 0;
@@ -766,9 +770,10 @@ __device__ __forceinline__ void decode_pipe_body(const DecodeArgs& a, const int 
         if (!a.pdl_early) pdl_trigger();
       }
     }
+    pdl_wait();  // outputs may alias the previous kernel's buffers
     __syncthreads();
     constexpr int kOut = RG * NT * 128;  // fragment elements of this CTA's sums
-    // sum over the consumer warps of fragment element idx (this CTA's K part)
+    // sum over the consumer warps of fragment element idx
     auto cta_sum = [&](int idx) {
         const int rgl = idx / (NT * 128);
         const int rem = idx % (NT * 128);
@@ -777,36 +782,16 @@ __device__ __forceinline__ void decode_pipe_body(const DecodeArgs& a, const int 
         for (int ww = 0; ww < kWarps; ++ww) v += red[(rgl * kWarps + ww) * NT * 128 + rem];
         return v;
     };
-    // K parts 1..KS-1 of the cluster: hand the sums to part 0 and finish
-    float* parts = red + RG * kWarps * NT * 128;  // (KS - 1) x kOut floats, read in part 0
-    if constexpr (KS > 1) {
-        cluster_wait();  // every CTA of the cluster has started (arrival at the top)
-        if (kpart != 0) {
-            const uint32_t dst = cluster_map(smem_u32(parts + (kpart - 1) * kOut), 0);
-            for (int idx = threadIdx.x; idx < kOut; idx += blockDim.x)
-                st_cluster_f32(dst + 4u * uint32_t(idx), cta_sum(idx));
-        }
-        cluster_arrive_release();
-        cluster_wait();
-        if (kpart != 0) return;
-    }
-    auto total = [&](int idx) {
-        float v = cta_sum(idx);
-#pragma unroll
-        for (int p = 1; p < KS; ++p) v += parts[(p - 1) * kOut + idx];
-        return v;
-    };
-    pdl_wait();  // outputs may alias the previous kernel's buffers
     for (int idx = threadIdx.x; idx < kOut; idx += blockDim.x) {
         const int rgl = idx / (NT * 128);
         const int rem = idx % (NT * 128);
         const int nb = rem >> 7, l = (rem >> 2) & 31, i = rem & 3;
         const int g = cta * RG + rgl;
-        float v = total(idx);
+        float v = cta_sum(idx);
         const int row = g * kRowGroup + (l >> 2) + 8 * (i >> 1);
         const int tok = 8 * nb + (l & 3) * 2 + (i & 1);
         if (a.act) {
-            if ((i >> 1) == 0 && g < a.groups) store_swiglu<B, HW>(a, g, l, tok, v, total(idx + 2));
+            if ((i >> 1) == 0 && g < a.groups) store_swiglu<B, HW>(a, g, l, tok, v, cta_sum(idx + 2));
             continue;
         }
         if (g < a.groups && row < a.N && tok < a.M) {
@@ -836,13 +821,9 @@ __device__ __forceinline__ void decode_pipe_body(const DecodeArgs& a, const int 
     }
 }
 
-// KS > 1 only in cluster launches of KS CTAs (consecutive blockIdx.x = one row-group CTA).
-template <int B, bool HW, int NT, bool DIRECT, int RG, int MINB, int TPW, int KS = 1>
+template <int B, bool HW, int NT, bool DIRECT, int RG, int MINB, int TPW>
 __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(DecodeArgs a) {
-    if constexpr (KS == 1)
-        decode_pipe_body<B, HW, NT, DIRECT, RG, TPW>(a, int(blockIdx.x));
-    else
-        decode_pipe_body<B, HW, NT, DIRECT, RG, TPW, KS>(a, int(blockIdx.x) / KS, int(blockIdx.x) % KS);
+    decode_pipe_body<B, HW, NT, DIRECT, RG, TPW>(a, int(blockIdx.x));
 }
 
 constexpr int kStages = 4;
@@ -926,16 +907,14 @@ cudaError_t launch_one(DecodeArgs& a, int groups, cudaStream_t s) {
     return launch_maybe_xchg(kern, a, unsigned(groups), kThreads, smem, s);
 }
 
-template <int B, bool HW, int NT, bool DIRECT, int RG, int TPW, int MINB = (RG == 1 ? 3 : 1),
-          int KS = 1>
+template <int B, bool HW, int NT, bool DIRECT, int RG, int TPW, int MINB = (RG == 1 ? 3 : 1)>
 cudaError_t launch_pipe(DecodeArgs& a, int groups, cudaStream_t s) {
     using S = PipeStage<B, NT, RG, TPW>;
     // MINB CTAs per SM share its shared memory (three: 27 warps; two: 18; RG == 2:
     // one CTA of 17 warps).  The ring is as deep as that budget allows for this M
-    // (2..kMaxStages stages).  KS > 1 adds the buffer that receives the other K
-    // parts' sums.
+    // (2..kMaxStages stages).
     constexpr int kBudget = MINB >= 4 ? 54 * 1024 : MINB == 3 ? 74 * 1024 : (MINB == 2 ? 110 * 1024 : 215 * 1024);
-    constexpr int kFixed = 2 * kMaxStages * 8 + S::kRedBytes + (KS - 1) * RG * NT * 128 * 4 + 16;
+    constexpr int kFixed = 2 * kMaxStages * 8 + S::kRedBytes + 16;
     const int mrows = a.M < NT * 8 ? a.M : NT * 8;
     a.stage_bytes = S::bytes(mrows);
     int D = (kBudget - kFixed) / a.stage_bytes;
@@ -943,7 +922,7 @@ cudaError_t launch_pipe(DecodeArgs& a, int groups, cudaStream_t s) {
     if (D < 2) return cudaErrorInvalidConfiguration;  // dispatch keeps every case >= 2 stages
     a.stages = D;
     const int smem = D * a.stage_bytes + kFixed;
-    auto kern = decode_pipe_kernel<B, HW, NT, DIRECT, RG, MINB, TPW, KS>;
+    auto kern = decode_pipe_kernel<B, HW, NT, DIRECT, RG, MINB, TPW>;
     static std::atomic<uint64_t> configured{0};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -954,28 +933,8 @@ cudaError_t launch_pipe(DecodeArgs& a, int groups, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         configured.fetch_or(bit);
     }
-    const unsigned ctas = unsigned((groups + RG - 1) / RG);
-    if constexpr (KS == 1) {
-        return launch_maybe_xchg(kern, a, ctas, kThreads * RG + 32, smem, s, true);
-    } else {
-        if (a.xa.world) return cudaErrorInvalidConfiguration;  // exchange launches take KS == 1
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(ctas * KS);
-        cfg.blockDim = dim3(kThreads * RG + 32);
-        cfg.dynamicSmemBytes = size_t(smem);
-        cfg.stream = s;
-        cudaLaunchAttribute attr[2];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = KS;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[1].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = a.kt <= 128 ? 2 : 1;
-        a.pdl_early = 0;
-        return cudaLaunchKernelEx(&cfg, kern, a);
-    }
+    return launch_maybe_xchg(kern, a, unsigned((groups + RG - 1) / RG), kThreads * RG + 32, smem, s,
+                             true);
 }
 
 // ---------------------------------------------------------------------------
@@ -1061,27 +1020,6 @@ cudaError_t launch_multi(MultiArgs& ma, int total_ctas, int max_kt, cudaStream_t
     return cudaLaunchKernelEx(&cfg, kern, ma);
 }
 
-// K parts per row-group CTA (cluster size) for a plane-decode launch of `ctas` CTAs of
-// `rounds` ring rounds each, MINB resident per SM.
-int pick_ks(const DecodeArgs& a, int ctas, int rounds, int minb) {
-    (void)ctas;
-    (void)rounds;
-    (void)minb;
-    if (a.xa.world) return 1;  // exchange launches are cooperative, one CTA per row group
-    return 1;
-}
-
-template <int B, bool HW, int NT, bool DIRECT, int RG, int TPW, int MINB>
-cudaError_t launch_pipe_ks(DecodeArgs& a, int groups, cudaStream_t s) {
-    const int ctas = (groups + RG - 1) / RG;
-    const int rounds = (a.kt + kWarps * TPW - 1) / (kWarps * TPW);
-    switch (pick_ks(a, ctas, rounds, MINB)) {
-        case 2: return launch_pipe<B, HW, NT, DIRECT, RG, TPW, MINB, 2>(a, groups, s);
-        case 4: return launch_pipe<B, HW, NT, DIRECT, RG, TPW, MINB, 4>(a, groups, s);
-        default: return launch_pipe<B, HW, NT, DIRECT, RG, TPW, MINB, 1>(a, groups, s);
-    }
-}
-
 template <int B, bool HW>
 cudaError_t dispatch_nt(DecodeArgs& a, int groups, bool pipe, bool direct, cudaStream_t s) {
     constexpr bool kPlane = plane_layout(B) || (B == 8 && HW);
@@ -1101,19 +1039,19 @@ cudaError_t dispatch_nt(DecodeArgs& a, int groups, bool pipe, bool direct, cudaS
             //    grid): 2.36 -> 2.92, 2.71 -> 2.92, 2.57 -> 3.39 TB/s.
             const bool two_per_sm = groups <= 2 * sm_count() && a.kt <= 128;
             if (a.M <= 8) {
-                if (two_per_sm) return launch_pipe_ks<B, HW, 1, false, 1, 2, 2>(a, groups, s);
+                if (two_per_sm) return launch_pipe<B, HW, 1, false, 1, 2, 2>(a, groups, s);
                 if (a.kt > 128)
-                    return a.M <= 4 ? launch_pipe_ks<B, HW, 1, false, 1, 2, 3>(a, groups, s)
-                                    : launch_pipe_ks<B, HW, 1, false, 1, 2, 2>(a, groups, s);
-                if (a.M == 1) return launch_pipe_ks<B, HW, 1, false, 1, 2, 3>(a, groups, s);
+                    return a.M <= 4 ? launch_pipe<B, HW, 1, false, 1, 2, 3>(a, groups, s)
+                                    : launch_pipe<B, HW, 1, false, 1, 2, 2>(a, groups, s);
+                if (a.M == 1) return launch_pipe<B, HW, 1, false, 1, 2, 3>(a, groups, s);
                 // (the fullPrecision operands need more registers than four CTAs per SM leave)
                 if (!HW)
-                    return a.M <= 4 ? launch_pipe_ks<B, HW, 1, false, 1, 2, 3>(a, groups, s)
-                                    : launch_pipe_ks<B, HW, 1, false, 1, 2, 2>(a, groups, s);
-                return launch_pipe_ks<B, HW, 1, false, 1, 1, 4>(a, groups, s);
+                    return a.M <= 4 ? launch_pipe<B, HW, 1, false, 1, 2, 3>(a, groups, s)
+                                    : launch_pipe<B, HW, 1, false, 1, 2, 2>(a, groups, s);
+                return launch_pipe<B, HW, 1, false, 1, 1, 4>(a, groups, s);
             }
-            if (HW && groups > 2 * sm_count()) return launch_pipe_ks<B, HW, 2, false, 2, 1, 2>(a, groups, s);
-            return launch_pipe_ks<B, HW, 2, false, 2, 2, 1>(a, groups, s);
+            if (HW && groups > 2 * sm_count()) return launch_pipe<B, HW, 2, false, 2, 1, 2>(a, groups, s);
+            return launch_pipe<B, HW, 2, false, 2, 2, 1>(a, groups, s);
         }
     }
     if (pipe) {

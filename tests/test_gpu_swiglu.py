@@ -23,8 +23,10 @@ def _pair(I, K, bits, seed):
     return out
 
 
-# K = 4096 / 520: pipelined and generic decode kernels; M up to 16
-@pytest.mark.parametrize("I,K,bits", [(512, 4096, 10), (136, 520, 11), (1792, 1024, 9)])
+# K = 4096 / 520: pipelined and generic decode kernels; M up to 16; 8192 x 4096 interleaved
+# rows (a grid of several waves)
+@pytest.mark.parametrize("I,K,bits", [(512, 4096, 10), (136, 520, 11), (1792, 1024, 9),
+                                        (4096, 4096, 10)])
 @pytest.mark.parametrize("M", [1, 5, 16])
 @pytest.mark.parametrize("with_bias", [False, True])
 def test_swiglu_matches_linear_then_activation(cuda_ok, I, K, bits, M, with_bias):
