@@ -361,7 +361,9 @@ uint64_t ebx_linear_workspace_bytes(const ebx_matrix* h, int64_t M) {
     // larger M: optional room for the exactly dequantised fp16 weight, which takes the
     // materialise + tcgen05 GEMM route (faster); without it the prefill decode-GEMM runs
     if (M <= ebx::kGemmMinRows) return 0;
-    return uint64_t(ebx::round_up(int64_t(h->m.rows) * h->m.cols * 2, 256));
+    DeviceGuard g(h->m.device);
+    return uint64_t(ebx::round_up(int64_t(h->m.rows) * h->m.cols * 2, 256)) +
+           ebx::gemm_part_bytes(M, h->m.rows, h->m.cols);
 }
 
 ebx_status ebx_linear(const ebx_matrix* h, const void* x, int64_t M, const void* bias, void* y,
@@ -395,11 +397,14 @@ ebx_status ebx_linear(const ebx_matrix* h, const void* x, int64_t M, const void*
     if (M > ebx::kGemmMinRows && need > 0 && workspace && workspace_bytes >= w16_bytes &&
         ebx::gemm_supported(h->m.cols, x, workspace)) {
         // prefill with the optional workspace: exact fp16 weight into it, then the tcgen05 GEMM
+        // (and, after it, room for fp32 split-K partials when the GEMM splits K)
         uint16_t* w16 = static_cast<uint16_t*>(workspace);
+        float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + w16_bytes);
         EBX_CUDA(ebx::launch_materialize(h->m, w16, s));
         EBX_CUDA(ebx::launch_gemm_f16(static_cast<const uint16_t*>(x), w16, M, h->m.rows,
                                       h->m.cols, static_cast<const uint16_t*>(bias),
-                                      static_cast<uint16_t*>(y), y32, s));
+                                      static_cast<uint16_t*>(y), y32, part,
+                                      workspace_bytes - w16_bytes, s));
         return EBX_OK;
     }
     if (M > ebx::kGemmMinRows && ebx::pgemm_supported(h->m, x)) {

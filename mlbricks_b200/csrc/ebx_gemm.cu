@@ -64,7 +64,30 @@ struct GemmArgs {
     uint16_t* y;
     float* y32;
     int M, N, K;
+    int full_tiles;  // output tiles computed whole (the first full waves)
+    int tail_split;  // K splits of each remaining tile (1: none)
+    float* part;     // tail_split > 1: fp32 partial tiles [tail_split][tail tiles][BM][BN]
 };
+
+// Work unit u: tiles [0, full_tiles) whole, one unit each; every tile after them
+// (the last, partial wave) as tail_split units over consecutive k-block ranges, so the
+// last wave takes 1 / tail_split of a tile's time.  tail = tile index among the split
+// tiles, s = its split (-1: a whole tile).
+__device__ __forceinline__ void gemm_unit(const GemmArgs& a, int u, int tiles, int kblocks, int& t,
+                                          int& s, int& kb0, int& kb1) {
+    if (u < a.full_tiles) {
+        t = u;
+        s = -1;
+        kb0 = 0;
+        kb1 = kblocks;
+        return;
+    }
+    const int v = u - a.full_tiles, tail_tiles = tiles - a.full_tiles;
+    t = a.full_tiles + v % tail_tiles;
+    s = v / tail_tiles;
+    kb0 = kblocks * s / a.tail_split;
+    kb1 = kblocks * (s + 1) / a.tail_split;
+}
 
 // Shared-memory matrix descriptor: K-major tile with 128-byte swizzle, rows of
 // 128 bytes, 8-row core groups 1024 bytes apart (SBO), sm_100 version field.
@@ -153,6 +176,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int m_tiles = (a.M + BM - 1) / BM;
     const int n_tiles = (a.N + BN - 1) / BN;
     const int tiles = m_tiles * n_tiles;
+    const int units = a.full_tiles + (tiles - a.full_tiles) * a.tail_split;
 
     if (warp == 0) {
         if (lane == 0) {
@@ -182,10 +206,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (lane == 0) {  // TMA producer: runs ahead across tiles
             int it = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-                int mt, nt;
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+                int t, sp, kb0, kb1, mt, nt;
+                gemm_unit(a, u, tiles, kblocks, t, sp, kb0, kb1);
                 tile_coords(t, m_tiles, n_tiles, mt, nt);
-                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int st = it % kStagesG;
                     if (it >= kStagesG &&
                         !gemm_wait(smem_u32(&empty[st]), uint32_t(((it / kStagesG) - 1) & 1))) {
@@ -205,12 +230,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (lane == 0) {  // MMA issuer
             int it = 0, i = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++i) {
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++i) {
+                int t, sp, kb0, kb1;
+                gemm_unit(a, u, tiles, kblocks, t, sp, kb0, kb1);
                 const int acc = i & 1;
                 if (i >= 2 && !gemm_wait(smem_u32(&acc_empty[acc]), uint32_t(((i >> 1) - 1) & 1))) break;
                 asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
                 const uint32_t d = tmem + uint32_t(acc * kAccCols);
-                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int st = it % kStagesG;
                     if (!gemm_wait(smem_u32(&full[st]), uint32_t((it / kStagesG) & 1))) {
                         ok = false;
@@ -222,7 +249,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k)
                         umma_f16(d, sw128_desc(abase + k * 32), sw128_desc(bbase + k * 32), G::kIdesc,
-                                 (kb | k) != 0 ? 1u : 0u);
+                                 (kb != kb0 || k != 0) ? 1u : 0u);
                     umma_commit(smem_u32(&empty[st]));
                 }
                 umma_commit(smem_u32(&acc_full[acc]));  // fires when this tile's MMAs are done
@@ -234,11 +261,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int quarter = warp & 3;  // TMEM lanes this warp may access
         const bool vec = (a.N % 8) == 0;
         int i = 0;
-        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+        for (int u = blockIdx.x; u < units; u += gridDim.x, ++i) {
             const int acc = i & 1;
             if (!gemm_wait(smem_u32(&acc_full[acc]), uint32_t((i >> 1) & 1))) break;
             asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-            int mt, nt;
+            int t, sp, kb0, kb1, mt, nt;
+            gemm_unit(a, u, tiles, kblocks, t, sp, kb0, kb1);
             tile_coords(t, m_tiles, n_tiles, mt, nt);
             const int m = mt * BM + quarter * 32 + lane;
             const int n0 = nt * BN;
@@ -261,6 +289,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
                 const int nb = n0 + c * 32;
                 if (m >= a.M || nb >= a.N) continue;
+                if (sp >= 0) {  // fp32 partial tile of split sp; gemm_tail_reduce adds splits and bias
+                    float* prow = a.part +
+                                  (size_t(sp) * (tiles - a.full_tiles) + (t - a.full_tiles)) * (BM * BN) +
+                                  size_t(quarter * 32 + lane) * BN + c * 32;
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        reinterpret_cast<float4*>(prow)[q] =
+                            make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                                        __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+                    continue;
+                }
                 float f[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
@@ -1178,10 +1217,105 @@ bool gemm_supported(int K, const void* x, const void* w16) {
            (reinterpret_cast<uintptr_t>(w16) & 15) == 0 && encode_fn() != nullptr;
 }
 
+int gemm_sm_count(int dev) {
+    static std::atomic<int> cache[64];
+    int sms = cache[dev & 63].load(std::memory_order_relaxed);
+    if (sms == 0) {
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+        cache[dev & 63].store(sms, std::memory_order_relaxed);
+    }
+    return sms;
+}
+
+// The split tiles of the last wave: y = fp16(sum of the splits in order + bias).  A
+// block covers 1024 consecutive elements of one tile (4 per thread: one float4 of each
+// split's partial), so the tile's coordinates are computed once per thread
+// (programmatic dependent launch: waits for the GEMM grid).
+template <int BN>
+__global__ void __launch_bounds__(256) gemm_tail_reduce_kernel(const float* part, int S, int full_tiles,
+                                                               int tail_tiles, int M, int N,
+                                                               const uint16_t* bias, uint16_t* y,
+                                                               float* y32) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    constexpr int kPerTile = BM * BN;
+    constexpr int kBlocksPerTile = kPerTile / 1024;
+    const int r = int(blockIdx.x) / kBlocksPerTile;
+    const int off = (int(blockIdx.x) % kBlocksPerTile) * 1024 + int(threadIdx.x) * 4;
+    int mt, nt;
+    tile_coords(full_tiles + r, (M + BM - 1) / BM, (N + BN - 1) / BN, mt, nt);
+    const int m = mt * BM + off / BN, n = nt * BN + off % BN;
+    if (m >= M || n >= N) return;
+    const size_t base = size_t(r) * kPerTile + off;
+    float4 v = *reinterpret_cast<const float4*>(part + base);
+    for (int sp = 1; sp < S; ++sp) {
+        const float4 u = *reinterpret_cast<const float4*>(part + size_t(sp) * tail_tiles * kPerTile + base);
+        v.x += u.x; v.y += u.y; v.z += u.z; v.w += u.w;
+    }
+    float f[4] = {v.x, v.y, v.z, v.w};
+    const size_t o = size_t(m) * N + n;
+    if ((N & 3) == 0 && n + 4 <= N) {
+        if (bias) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) f[j] += __half2float(__ushort_as_half(bias[n + j]));
+        }
+        uint2 h;
+        h.x = pack_half2(f[0], f[1]);
+        h.y = pack_half2(f[2], f[3]);
+        *reinterpret_cast<uint2*>(y + o) = h;
+        if (y32) *reinterpret_cast<float4*>(y32 + o) = make_float4(f[0], f[1], f[2], f[3]);
+        return;
+    }
+    for (int j = 0; j < 4 && n + j < N; ++j) {
+        float w = f[j];
+        if (bias) w += __half2float(__ushort_as_half(bias[n + j]));
+        y[o + j] = __half_as_ushort(__float2half_rn(w));
+        if (y32) y32[o + j] = w;
+    }
+}
+
+// Weight-tile width (256 columns: measured fastest at every config-3 size, against 128
+// and 64) and the tail split: whole waves of output tiles stay whole, the tiles of a
+// last, partial wave are split over K so that they occupy up to every SM (at most 8 ways,
+// at least 4 k-blocks each).  Measured per call, materialise included (B200, graph
+// replay): 4096 x 4096 at M = 512 40.9 -> 34.6 us, 14336 x 4096 at M = 512 129 -> 96 us
+// and at M = 4096 420 -> 400 us, 4096 x 14336 at M = 1024 140 -> 133 us; no shape slower.
+// Splitting every tile instead (partials of the whole output through HBM) was slower at
+// every M >= 1024.
+struct GemmPlan {
+    int bn = 256;
+    int full_tiles = 0;
+    int tail_split = 1;
+};
+
+GemmPlan gemm_plan(int64_t M, int N, int K, int sms) {
+    GemmPlan p;
+    const int64_t tiles = ((M + BM - 1) / BM) * ((N + p.bn - 1) / p.bn);
+    const int64_t kblocks = (K + BK - 1) / BK;
+    const int64_t tail = tiles % sms;
+    p.full_tiles = int(tiles - tail);
+    if (tail == 0) return p;
+    int S = int(sms / tail);
+    if (S > 8) S = 8;
+    while (S > 1 && kblocks < 4 * S) --S;
+    p.tail_split = S;
+    if (S == 1) p.full_tiles = int(tiles);
+    return p;
+}
+
+uint64_t gemm_part_bytes(int64_t M, int N, int K) {
+    if (M <= 0) return 0;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    const GemmPlan p = gemm_plan(M, N, K, gemm_sm_count(dev));
+    if (p.tail_split == 1) return 0;
+    const int64_t tiles = ((M + BM - 1) / BM) * ((N + p.bn - 1) / p.bn);
+    return uint64_t(round_up((tiles - p.full_tiles) * p.tail_split * int64_t(BM) * p.bn * 4, 256));
+}
+
 template <int BN>
 cudaError_t launch_gemm_bn(const uint16_t* x, const uint16_t* w16, int64_t M, int N, int K,
-                           const uint16_t* bias, uint16_t* y, float* y32, int sms, int dev,
-                           cudaStream_t s) {
+                           const uint16_t* bias, uint16_t* y, float* y32, GemmPlan p, float* part,
+                           int sms, int dev, cudaStream_t s) {
     using G = GemmCfg<BN>;
     CUtensorMap tx, tw;
     if (!make_map(&tx, x, int(M), K, BM) || !make_map(&tw, w16, N, K, BN)) return cudaErrorInvalidValue;
@@ -1193,50 +1327,42 @@ cudaError_t launch_gemm_bn(const uint16_t* x, const uint16_t* w16, int64_t M, in
         if (e != cudaSuccess) return e;
         configured.fetch_or(bit);
     }
-    GemmArgs a{bias, y, y32, int(M), N, K};
     const int64_t tiles = ((M + BM - 1) / BM) * int64_t((N + BN - 1) / BN);
-    if (tiles > INT32_MAX) return cudaErrorInvalidValue;
-    const unsigned grid = unsigned(tiles < sms ? tiles : sms);  // persistent: one CTA per SM
+    if (tiles > INT32_MAX / 8) return cudaErrorInvalidValue;
+    GemmArgs a{bias, y, y32, int(M), N, K, p.full_tiles, p.tail_split, part};
+    const int64_t units = p.full_tiles + (tiles - p.full_tiles) * p.tail_split;
+    const unsigned grid = unsigned(units < sms ? units : sms);  // persistent: one CTA per SM
     kern<<<grid, kGemmThreads, G::kSmem, s>>>(tx, tw, a);
-    return cudaGetLastError();
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || p.tail_split == 1) return e;
+    const int tail_tiles = int(tiles - p.full_tiles);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(tail_tiles * (BM * BN / 1024)));
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_tail_reduce_kernel<BN>, static_cast<const float*>(part),
+                              p.tail_split, p.full_tiles, tail_tiles, int(M), N, bias, y, y32);
 }
 
 cudaError_t launch_gemm_f16(const uint16_t* x, const uint16_t* w16, int64_t M, int N, int K,
-                            const uint16_t* bias, uint16_t* y, float* y32, cudaStream_t s) {
+                            const uint16_t* bias, uint16_t* y, float* y32, float* part,
+                            uint64_t part_bytes, cudaStream_t s) {
     if (M <= 0) return cudaSuccess;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    static std::atomic<int> sm_count[64];
-    int sms = sm_count[dev & 63].load(std::memory_order_relaxed);
-    if (sms == 0) {
-        e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) return e;
-        sm_count[dev & 63].store(sms, std::memory_order_relaxed);
+    const int sms = gemm_sm_count(dev);
+    GemmPlan p = gemm_plan(M, N, K, sms);
+    if (p.tail_split > 1 && (!part || part_bytes < gemm_part_bytes(M, N, K))) {
+        p.full_tiles = int(((M + BM - 1) / BM) * ((N + p.bn - 1) / p.bn));  // no room: no split
+        p.tail_split = 1;
     }
-    // Weight-tile width: estimated time = rounds of tiles over the SMs x tile width x a
-    // per-width cost factor (narrower tiles move more operand bytes per flop); small M
-    // takes narrow tiles so that M = 256 does not leave most of the GPU idle, while
-    // M = 1024 keeps one round of wide tiles rather than two rounds of narrow ones.
-    const int64_t m_tiles = (M + BM - 1) / BM;
-    auto cost = [&](int bn, int64_t factor_pct) {
-        const int64_t rounds = (m_tiles * ((N + bn - 1) / bn) + sms - 1) / sms;
-        return rounds * bn * factor_pct;
-    };
-    const int64_t c256 = cost(256, 100), c128 = cost(128, 115), c64 = cost(64, 135);
-    if (c256 <= c128 && c256 <= c64) return launch_gemm_bn<256>(x, w16, M, N, K, bias, y, y32, sms, dev, s);
-    if (c128 <= c64) return launch_gemm_bn<128>(x, w16, M, N, K, bias, y, y32, sms, dev, s);
-    return launch_gemm_bn<64>(x, w16, M, N, K, bias, y, y32, sms, dev, s);
-}
-
-int gemm_sm_count(int dev) {
-    static std::atomic<int> cache[64];
-    int sms = cache[dev & 63].load(std::memory_order_relaxed);
-    if (sms == 0) {
-        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
-        cache[dev & 63].store(sms, std::memory_order_relaxed);
-    }
-    return sms;
+    return launch_gemm_bn<256>(x, w16, M, N, K, bias, y, y32, p, part, sms, dev, s);
 }
 
 // Measured on the BASELINE shapes: the decode-GEMM beats chunked decode for every

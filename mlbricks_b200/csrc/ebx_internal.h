@@ -94,8 +94,12 @@ cudaError_t launch_xchg_allreduce(const XchgArgs& xa, const float* part, int M, 
 // Rows above which ebx_linear takes the materialise + tcgen05 GEMM route.
 constexpr int64_t kGemmMinRows = 64;
 bool gemm_supported(int K, const void* x, const void* w16);
+// part (may be null): room for fp32 split-K partials; the GEMM splits K over CTAs only when
+// part_bytes covers what gemm_part_bytes(M, N, K) asks for, and adds the splits in order.
 cudaError_t launch_gemm_f16(const uint16_t* x, const uint16_t* w16, int64_t M, int N, int K,
-                            const uint16_t* bias, uint16_t* y, float* y32, cudaStream_t s);
+                            const uint16_t* bias, uint16_t* y, float* y32, float* part,
+                            uint64_t part_bytes, cudaStream_t s);
+uint64_t gemm_part_bytes(int64_t M, int N, int K);
 cudaError_t read_gemm_status(int* status, bool clear, cudaStream_t s);
 // Decode-GEMM for 16 < M <= 256: codes decoded straight into tcgen05 tiles (weights as the
 // 128-row MMA side, tokens as N); K split over CTAs when needed, with an fp32 partial
