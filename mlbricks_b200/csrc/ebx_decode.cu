@@ -517,7 +517,6 @@ __device__ __forceinline__ void decode_pipe_body(const DecodeArgs& a, const int 
     const int lane = threadIdx.x & 31;
     const int rounds = (a.kt + S::kRound - 1) / S::kRound;
     const int mrows = a.M < NT * 8 ? a.M : NT * 8;
-    const uint32_t xe = a.xa.world ? xchg_epoch(a.xa) + 1u : 0u;  // epoch this call publishes
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < D; ++i) {
@@ -772,6 +771,9 @@ __device__ __forceinline__ void decode_pipe_body(const DecodeArgs& a, const int 
     }
     pdl_wait();  // outputs may alias the previous kernel's buffers
     __syncthreads();
+    // epoch this call publishes: read after griddepcontrol.wait, so a previous exchange
+    // call on the same stream has completed and advanced it
+    const uint32_t xe = a.xa.world ? xchg_epoch(a.xa) + 1u : 0u;
     constexpr int kOut = RG * NT * 128;  // fragment elements of this CTA's sums
     // sum over the consumer warps of fragment element idx
     auto cta_sum = [&](int idx) {
@@ -878,11 +880,17 @@ cudaError_t launch_maybe_xchg(Kern kern, DecodeArgs& a, unsigned grid, unsigned 
     cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = size_t(smem);
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    // pdl (pipe kernel): the next kernel's weight prefetch may overlap this one's
+    // exchange, and this one's the previous kernel's tail (it reads the exchange epoch,
+    // the activations and its outputs' memory only after griddepcontrol.wait)
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = a.xa.fused ? 1 : 0;
+    cfg.numAttrs = a.xa.fused ? (pdl ? 2 : 1) : 0;
+    a.pdl_early = 0;
     return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
