@@ -752,8 +752,11 @@ def run_prefill(mats, device, lib, args) -> dict:
 
     sel = [e for e in mats if e["threshold"] == 0.01]
     pk = peaks()
-    maxws = max(e["N"] * e["K"] * 2 for e in sel)
-    ws = torch.empty(maxws + 256, dtype=torch.uint8, device=device)
+    # one workspace as large as the largest that ebx_linear_workspace_bytes asks for (the
+    # fp16 weight and, when the GEMM splits its last wave, the fp32 partial tiles)
+    maxws = max(int(lib.ebx_linear_workspace_bytes(ctypes.c_void_p(e["matrix"]._native.handle), M))
+                for e in sel for M in PREFILL_MS)
+    ws = torch.empty(max(maxws, 256), dtype=torch.uint8, device=device)
     cases = []
     for M in PREFILL_MS:
         xs = {e["K"]: torch.randn((M, e["K"]), device=device, dtype=torch.float16) for e in sel}

@@ -346,10 +346,17 @@ struct PipeStage {
     static constexpr int kRound = kWarps * TPW;                // supertiles per round and row group
     static constexpr int kWBytes = kRound * kTileBytes;        // one row group's round
     static constexpr int kXStride = kRound * kKTile * 2 + 16;  // bank-shifted activation rows
+    // the consumers' fragment sums, written over the (drained) ring after the main loop
     static constexpr int kRedBytes = RG * kWarps * NT * 128 * 4;
-    // stage = RG weight rounds + activation rows of tokens 0..m-1 + one zero row
-    static int bytes(int m) { return RG * kWBytes + (m + 1) * kXStride; }
+    // stage = RG weight rounds + activation rows of tokens 0..m-1, and one zero row read
+    // by the lanes whose token is >= m when m < 8 NT
+    static int bytes(int m) { return RG * kWBytes + (m + (m < NT * 8 ? 1 : 0)) * kXStride; }
 };
+
+// Barrier 1 over the `warps` consumer warps (the producer warp does not take part).
+__device__ __forceinline__ void consumers_sync(int warps) {
+    asm volatile("bar.sync 1, %0;" ::"r"(warps * 32) : "memory");
+}
 
 // Programmatic dependent launch (no-ops when the launch did not ask for it):
 // griddepcontrol.wait blocks until the previous kernel in the stream has
@@ -488,6 +495,7 @@ __device__ __forceinline__ void plane_consume(const DecodeArgs& a, uint8_t* smem
             ph ^= 1u;
         }
     }
+    consumers_sync(RG * kWarps);  // red[] lies over the ring: every consumer is done with it
 #pragma unroll
     for (int nb = 0; nb < NT; ++nb)
 #pragma unroll
@@ -512,7 +520,7 @@ __device__ __forceinline__ void decode_pipe_body(const DecodeArgs& a, const int 
     const int SB = a.stage_bytes;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + D * SB);
     uint64_t* empty = full + kMaxStages;
-    float* red = reinterpret_cast<float*>(empty + kMaxStages);
+    float* red = reinterpret_cast<float*>(smem);  // over the ring once every consumer is done
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int rounds = (a.kt + S::kRound - 1) / S::kRound;
@@ -526,10 +534,11 @@ __device__ __forceinline__ void decode_pipe_body(const DecodeArgs& a, const int 
     }
     // zero row (index mrows) of every stage, never written by the copy engine:
     // lanes whose token is >= M read it
-    for (int i = threadIdx.x; i < D * (S::kXStride / 16); i += blockDim.x)
-        *reinterpret_cast<uint4*>(smem + (i / (S::kXStride / 16)) * SB + RG * S::kWBytes +
-                                  mrows * S::kXStride + (i % (S::kXStride / 16)) * 16) =
-            make_uint4(0, 0, 0, 0);
+    if (mrows < NT * 8)
+        for (int i = threadIdx.x; i < D * (S::kXStride / 16); i += blockDim.x)
+            *reinterpret_cast<uint4*>(smem + (i / (S::kXStride / 16)) * SB + RG * S::kWBytes +
+                                      mrows * S::kXStride + (i % (S::kXStride / 16)) * 16) =
+                make_uint4(0, 0, 0, 0);
     fence_proxy_async_smem();
     __syncthreads();
 
@@ -761,6 +770,7 @@ __device__ __forceinline__ void decode_pipe_body(const DecodeArgs& a, const int 
                 ph ^= 1u;
             }
         }
+        consumers_sync(kConsumers);  // red[] lies over the ring: every consumer is done with it
 #pragma unroll
         for (int nb = 0; nb < NT; ++nb)
 #pragma unroll
@@ -829,6 +839,12 @@ __global__ void __launch_bounds__(kThreads * RG + 32, MINB) decode_pipe_kernel(D
 }
 
 constexpr int kStages = 4;
+
+// Dynamic shared memory of one pipe-kernel CTA when MINB of them share an SM: the SM's
+// 228 KB less 1 KB reserved per CTA, split evenly (227 KB for one CTA).
+constexpr int pipe_smem_budget(int minb) {
+    return minb >= 4 ? 56 * 1024 : minb == 3 ? 75 * 1024 : minb == 2 ? 113 * 1024 : 227 * 1024;
+}
 
 // Multiprocessors of the current device (cached per device).
 int sm_count() {
@@ -916,18 +932,19 @@ cudaError_t launch_one(DecodeArgs& a, int groups, cudaStream_t s) {
 }
 
 template <int B, bool HW, int NT, bool DIRECT, int RG, int TPW, int MINB = (RG == 1 ? 3 : 1)>
-cudaError_t launch_pipe(DecodeArgs& a, int groups, cudaStream_t s) {
+cudaError_t launch_pipe(DecodeArgs& a, int groups, cudaStream_t s, int max_stages = kMaxStages) {
     using S = PipeStage<B, NT, RG, TPW>;
     // MINB CTAs per SM share its shared memory (three: 27 warps; two: 18; RG == 2:
     // one CTA of 17 warps).  The ring is as deep as that budget allows for this M
     // (2..kMaxStages stages).
-    constexpr int kBudget = MINB >= 4 ? 54 * 1024 : MINB == 3 ? 74 * 1024 : (MINB == 2 ? 110 * 1024 : 215 * 1024);
-    constexpr int kFixed = 2 * kMaxStages * 8 + S::kRedBytes + 16;
+    constexpr int kBudget = pipe_smem_budget(MINB);
+    constexpr int kFixed = 2 * kMaxStages * 8 + 16;  // barriers; red[] reuses the ring
     const int mrows = a.M < NT * 8 ? a.M : NT * 8;
     a.stage_bytes = S::bytes(mrows);
     int D = (kBudget - kFixed) / a.stage_bytes;
-    D = D > kMaxStages ? kMaxStages : D;
-    if (D < 2) return cudaErrorInvalidConfiguration;  // dispatch keeps every case >= 2 stages
+    D = D > max_stages ? max_stages : D;
+    if (D < 2 || D * a.stage_bytes < S::kRedBytes)  // dispatch keeps every case >= 2 stages
+        return cudaErrorInvalidConfiguration;
     a.stages = D;
     const int smem = D * a.stage_bytes + kFixed;
     auto kern = decode_pipe_kernel<B, HW, NT, DIRECT, RG, MINB, TPW>;
@@ -987,8 +1004,8 @@ __global__ void __launch_bounds__(kThreads + 32, MINB) decode_multi_kernel(const
 
 template <int NT, int TPW, int MINB>
 cudaError_t launch_multi(MultiArgs& ma, int total_ctas, int max_kt, cudaStream_t s) {
-    constexpr int kBudget = MINB == 3 ? 74 * 1024 : 110 * 1024;
-    constexpr int kFixed = 2 * kMaxStages * 8 + kWarps * NT * 128 * 4 + 16;
+    constexpr int kBudget = pipe_smem_budget(MINB);
+    constexpr int kFixed = 2 * kMaxStages * 8 + 16;  // barriers; red[] reuses the ring
     int smem = 0;
     for (int i = 0; i < ma.count; ++i) {
         DecodeArgs& a = ma.m[i];
@@ -996,10 +1013,10 @@ cudaError_t launch_multi(MultiArgs& ma, int total_ctas, int max_kt, cudaStream_t
         const int mrows = a.M < NT * 8 ? a.M : NT * 8;
         const int wbytes = kWarps * TPW * bits * 128;
         const int xstride = kWarps * TPW * kKTile * 2 + 16;
-        a.stage_bytes = wbytes + (mrows + 1) * xstride;
+        a.stage_bytes = wbytes + (mrows + (mrows < NT * 8 ? 1 : 0)) * xstride;
         int D = (kBudget - kFixed) / a.stage_bytes;
         D = D > kMaxStages ? kMaxStages : D;
-        if (D < 2) return cudaErrorInvalidConfiguration;
+        if (D < 2 || D * a.stage_bytes < kWarps * NT * 128 * 4) return cudaErrorInvalidConfiguration;
         a.stages = D;
         const int need = D * a.stage_bytes + kFixed;
         smem = need > smem ? need : smem;
@@ -1041,24 +1058,29 @@ cudaError_t dispatch_nt(DecodeArgs& a, int groups, bool pipe, bool direct, cudaS
             //    per warp and round at M = 1, four CTAs with one supertile for 1 < M <= 8
             //    (4.41 vs 4.26 TB/s at M = 2, 3.98 vs 3.60 at M = 8);
             //  * K = 14336 (few, long CTAs): three CTAs per SM at M <= 4, two at M <= 8;
-            //  * 8 < M <= 16: two row groups per CTA sharing each activation stage, which
-            //    halves the activation bytes staged per weight byte (1 CTA per SM with a
-            //    deep ring, or two CTAs with one supertile per warp for the 896-group
-            //    grid): 2.36 -> 2.92, 2.71 -> 2.92, 2.57 -> 3.39 TB/s.
+            //  * 8 < M <= 16: integer codes, one row group per CTA and two CTAs per SM;
+            //    fullPrecision, two row groups per CTA sharing each activation stage
+            //    (halves the activation bytes staged per weight byte).
+            // The consumers' sums go over the drained ring (no separate buffer) and the
+            // zero activation row exists only when M < 8 NT, which buys a stage at M = 16.
             const bool two_per_sm = groups <= 2 * sm_count() && a.kt <= 128;
             if (a.M <= 8) {
                 if (two_per_sm) return launch_pipe<B, HW, 1, false, 1, 2, 2>(a, groups, s);
                 if (a.kt > 128)
                     return a.M <= 4 ? launch_pipe<B, HW, 1, false, 1, 2, 3>(a, groups, s)
                                     : launch_pipe<B, HW, 1, false, 1, 2, 2>(a, groups, s);
-                if (a.M == 1) return launch_pipe<B, HW, 1, false, 1, 2, 3>(a, groups, s);
+                // (a two-stage ring: three stages measured 13 % slower on 4096 x 14336)
+                if (a.M == 1) return launch_pipe<B, HW, 1, false, 1, 2, 3>(a, groups, s, 2);
                 // (the fullPrecision operands need more registers than four CTAs per SM leave)
                 if (!HW)
                     return a.M <= 4 ? launch_pipe<B, HW, 1, false, 1, 2, 3>(a, groups, s)
                                     : launch_pipe<B, HW, 1, false, 1, 2, 2>(a, groups, s);
                 return launch_pipe<B, HW, 1, false, 1, 1, 4>(a, groups, s);
             }
-            if (HW && groups > 2 * sm_count()) return launch_pipe<B, HW, 2, false, 2, 1, 2>(a, groups, s);
+            // 8 < M <= 16, integer codes: one row group per CTA, two supertiles per warp and
+            // round, two CTAs per SM (measured against two row groups sharing activation
+            // stages: 6.8 -> 6.4, 24.4 -> 23.5, 23.2 -> 22.6 us on the three shapes)
+            if (HW) return launch_pipe<B, HW, 2, false, 1, 2, 2>(a, groups, s);
             return launch_pipe<B, HW, 2, false, 2, 2, 1>(a, groups, s);
         }
     }
