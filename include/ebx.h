@@ -114,12 +114,15 @@ EBX_API ebx_status ebx_matrix_materialize(const ebx_matrix* m, void* dst, void* 
 
 /* Workspace bytes ebx_linear asks for with M activation rows (0 when none):
  * the decode-GEMM's fp32 split-K partials for 16 < M <= 256 (required when
- * nonzero), and for larger M room for the exactly dequantised fp16 weight --
+ * nonzero), and for larger M room for the exactly dequantised fp16 weight
+ * followed by the fp32 partial tiles of the GEMM's split last wave --
  * optional: with it the prefill takes materialise + tcgen05 GEMM (the faster
  * route; fp16(q*s) operands, the reference's prefill arithmetic, whatever the
- * execution width), without it (NULL or smaller) the prefill decode-GEMM, which
- * decodes the codes into shared memory per k-block, needs no memory at all and
- * keeps the execution width's semantics. */
+ * execution width; given only the fp16 weight's rows*cols*2 bytes, rounded up to
+ * 256, the GEMM runs without the split), without it (NULL or smaller) the
+ * prefill decode-GEMM, which decodes the codes into shared memory per k-block,
+ * needs no memory at all and keeps the execution width's semantics.  The
+ * workspace_bytes passed to ebx_linear must not exceed the buffer's size. */
 EBX_API uint64_t ebx_linear_workspace_bytes(const ebx_matrix* m, int64_t M);
 
 /* y[M, rows] = x[M, cols] * W^T (+ bias), all fp16 DEVICE pointers, row-major,
