@@ -711,6 +711,8 @@ def run_tp_stack(args, world: int, rank: int, device) -> dict:
     # (fp32 partials stored into every rank's region over NVLink); larger M: NCCL
     exchange = (tp.Exchange.from_group(64, 4096)
                 if world > 1 and not getattr(args, "nccl_only", False) else None)
+    if exchange is not None:
+        exchange.set_protocol(getattr(args, "exchange_protocol", "auto"))
     layers, head, bits_of = build_stack(device, world, rank, coll, exchange)
     out = {"workload": "config5: 32 x (QKV 4096->6144 col, O 4096->4096 row, gate/up 4096->14336 "
                        "col, down 14336->4096 row) + lm_head 4096->128256 col, threshold 0.01; "
@@ -722,6 +724,10 @@ def run_tp_stack(args, world: int, rank: int, device) -> dict:
                        "integer-code semantics pinned on every rank; greedy ids by a distributed argmax "
                        "over the lm_head shards; one CUDA graph per decode step",
            "bits": bits_of}
+    if exchange is not None:
+        out["exchange_protocol"] = (getattr(args, "exchange_protocol", "auto") +
+                                    " (auto: two-phase owner reduce once world x M >= 48, "
+                                    "broadcast below)")
     out["parity"] = tp_parity(layers, head, bits_of, world, rank, device, coll)
     if world > 1:
         dist.barrier()
@@ -1228,6 +1234,8 @@ def main() -> None:
                     help="skip the reference's own CUDA path on the same sweep")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-tp-stack", action="store_true")
+    ap.add_argument("--exchange-protocol", default="auto", choices=["auto", "broadcast", "two_phase"],
+                    help="libebx exchange protocol of the tensor-parallel stack")
     ap.add_argument("--no-bolt", action="store_true", help="skip the config-4 decoder")
     ap.add_argument("--bolt-only", action="store_true", help="run only the config-4 decoder")
     ap.add_argument("--nccl-only", action="store_true",

@@ -245,12 +245,18 @@ EBX_API ebx_status ebx_linear_multi(const ebx_matrix* const* mats, int32_t count
  *   2. the caller all-gathers the blobs (any host transport) and passes all
  *      of them, in rank order, to ebx_exchange_connect, which maps every
  *      peer's region (cudaIpcOpenMemHandle);
- *   3. ebx_linear_allreduce: the shard's decode kernel stores its fp32
- *      partial sums straight into every rank's region and, once all of its
- *      CTAs are done, publishes an epoch flag to every rank (release, system
- *      scope); a finish kernel waits (bounded, ~2 s) for the flags of all
- *      ranks, sums the partials in rank order 0..world-1, adds bias in fp32
- *      and rounds once to fp16.  Every rank gets bit-identical outputs.
+ *   3. ebx_linear_allreduce: the shard's decode kernel stores each fp32
+ *      partial sum, tagged with the exchange's epoch in the same 8-byte word,
+ *      into the regions of the ranks that need it; readers poll the words
+ *      themselves (bounded, ~2 s), sum all ranks' partials in rank order
+ *      0..world-1, add bias in fp32 and round once to fp16.  Every rank gets
+ *      bit-identical outputs.  When the grid fits on the GPU this all happens
+ *      inside the decode launch (cooperative); otherwise a finish kernel sums.
+ *      Two protocols (ebx_exchange_set_protocol): broadcast -- every partial
+ *      into every rank's region, one hop, world x M x N words per rank -- and
+ *      two-phase -- each output's partials to one owner rank, which sums them
+ *      and stores the sum into every other rank's region, about 2 x M x N words
+ *      per rank for a second hop.  Both give the same bits.
  *
  * All ranks must issue the same sequence of ebx_linear_allreduce calls, each
  * call with the same M and shard shape on every rank; M and the shard's rows
@@ -281,12 +287,22 @@ EBX_API ebx_status ebx_linear_allreduce(const ebx_matrix* m, const void* x, int6
                                         const void* bias, void* y, float* y32, ebx_exchange* ex,
                                         void* stream);
 
+/* Exchange protocol for this rank's later calls (every rank must choose the same):
+ * EBX_EXCHANGE_AUTO (the default: two-phase once world * M >= 48, broadcast
+ * below), EBX_EXCHANGE_BROADCAST or EBX_EXCHANGE_TWO_PHASE.  The two-phase form
+ * applies to ebx_exchange_allreduce and to ebx_linear_allreduce launches whose
+ * grid fits on the GPU; the others broadcast.  No reference counterpart. */
+#define EBX_EXCHANGE_AUTO 0
+#define EBX_EXCHANGE_BROADCAST 1
+#define EBX_EXCHANGE_TWO_PHASE 2
+EBX_API ebx_status ebx_exchange_set_protocol(ebx_exchange* ex, int32_t protocol);
+
 /* y[M, N] (fp16) = fp16( sum over ranks of partial_r + bias ) for an fp32 partial
  * [M, N] this rank already holds -- a row-parallel shard's fp32 output from
  * ebx_linear (y32) at batch sizes above ebx_linear_allreduce's 16 rows -- over the
- * same exchange: one cooperative launch stores every element into every rank's
- * region and sums all ranks' words in rank order (bit-identical on every rank),
- * replacing an NCCL all-reduce of the partials.  M <= max_m, N <= max_n; bias (fp16,
+ * same exchange: one cooperative launch exchanges the elements (broadcast or
+ * two-phase, as above) and sums all ranks' words in rank order (bit-identical on
+ * every rank), replacing an NCCL all-reduce of the partials.  M <= max_m, N <= max_n; bias (fp16,
  * may be NULL), y32 (fp32 copy before rounding, may be NULL).  The same call-order
  * rules as ebx_linear_allreduce; no reference counterpart. */
 EBX_API ebx_status ebx_exchange_allreduce(ebx_exchange* ex, const float* partial, int64_t M,

@@ -80,6 +80,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ebx_exchange_destroy": (_ST, [_P]),
     "ebx_linear_allreduce": (_ST, [_P, _P, _I64, _P, _P, _P, _P, _P]),
     "ebx_exchange_allreduce": (_ST, [_P, _P, _I64, _I64, _P, _P, _P, _P]),
+    "ebx_exchange_set_protocol": (_ST, [_P, _I32]),
     "ebx_elastic_linear_packed": (
         _ST, [_P, _I32, _I64, _P, _P, _I32, _P, _I32, _I64, _I64, _I64, _P, _P]),
 }

@@ -661,6 +661,20 @@ ebx_status ebx_linear_allreduce(const ebx_matrix* h, const void* x, int64_t M, c
     return EBX_OK;
 }
 
+ebx_status ebx_exchange_set_protocol(ebx_exchange* ex, int32_t protocol) {
+    if (!ex) {
+        set_error("null argument");
+        return EBX_ERR_INVALID;
+    }
+    if (protocol < EBX_EXCHANGE_AUTO || protocol > EBX_EXCHANGE_TWO_PHASE) {
+        set_error("ebx_exchange_set_protocol: protocol must be EBX_EXCHANGE_AUTO, "
+                  "EBX_EXCHANGE_BROADCAST or EBX_EXCHANGE_TWO_PHASE");
+        return EBX_ERR_INVALID;
+    }
+    ex->xa.protocol = protocol;
+    return EBX_OK;
+}
+
 ebx_status ebx_exchange_allreduce(ebx_exchange* ex, const float* partial, int64_t M, int64_t N,
                                   const void* bias, void* y, float* y32, void* stream) {
     if (!ex || (M > 0 && N > 0 && (!partial || !y))) {

@@ -87,9 +87,13 @@ __device__ __forceinline__ void store_swiglu(const DecodeArgs& a, int g, int l, 
 }
 
 // Fused exchange: all ranks' partials of (tok, row) -> bias -> one fp16 rounding.
-__device__ __forceinline__ void xchg_finish_one(const DecodeArgs& a, uint32_t e, int tok, int row) {
+// owner >= 0: the two-phase form (the owner rank reduces, the others wait for its sum).
+__device__ __forceinline__ void xchg_finish_one(const DecodeArgs& a, uint32_t e, int tok, int row,
+                                                int owner = -1) {
     float v;
-    if (!xchg_gather(a.xa, e, a.M, a.N, tok, row, v)) {
+    const bool ok = owner >= 0 ? xchg_reduce_owner(a.xa, e, owner, a.M, a.N, tok, row, v)
+                               : xchg_gather(a.xa, e, a.M, a.N, tok, row, v);
+    if (!ok) {
         atomicExch(&g_device_status, kXchgTimeout);
         return;
     }
@@ -808,7 +812,9 @@ __device__ __forceinline__ void decode_pipe_body(const DecodeArgs& a, const int 
         }
         if (g < a.groups && row < a.N && tok < a.M) {
             if constexpr (HW && B != kFp16Bits) v = v * a.scales[row];
-            if (a.xa.world) {
+            if (a.xa.two_phase) {
+                xchg_push_owner(a.xa, xe, xchg_owner(a.xa, g, a.groups), a.N, tok, row, v);
+            } else if (a.xa.world) {
                 xchg_push(a.xa, xe, a.M, a.N, tok, row, v);
             } else {
                 if (a.bias) v += __half2float(__ushort_as_half(a.bias[row]));
@@ -827,7 +833,8 @@ __device__ __forceinline__ void decode_pipe_body(const DecodeArgs& a, const int 
             const int g = cta * RG + rgl;
             const int row = g * kRowGroup + (l >> 2) + 8 * (i >> 1);
             const int tok = 8 * nb + (l & 3) * 2 + (i & 1);
-            if (g < a.groups && row < a.N && tok < a.M) xchg_finish_one(a, xe, tok, row);
+            if (g < a.groups && row < a.N && tok < a.M)
+                xchg_finish_one(a, xe, tok, row, a.xa.two_phase ? xchg_owner(a.xa, g, a.groups) : -1);
         }
         xchg_advance(a.xa, xe);
     }
@@ -865,7 +872,7 @@ int sm_count() {
 // never hold back CTAs of their own grid that those peers wait for in turn.
 template <typename Kern>
 cudaError_t launch_maybe_xchg(Kern kern, DecodeArgs& a, unsigned grid, unsigned threads, int smem,
-                              cudaStream_t s, bool pdl = false) {
+                              cudaStream_t s, bool pdl = false, bool two_phase_ok = false) {
     if (!a.xa.world) {
         // pdl: the kernel waits (griddepcontrol.wait) before it reads anything the
         // previous kernel may write, so it may be launched before that one completes
@@ -891,6 +898,8 @@ cudaError_t launch_maybe_xchg(Kern kern, DecodeArgs& a, unsigned grid, unsigned 
         e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, int(threads), size_t(smem));
     if (e != cudaSuccess) return e;
     a.xa.fused = int64_t(grid) <= int64_t(per_sm) * sms ? 1 : 0;
+    // owner reduce + owner broadcast (fused launches of the pipe kernel only)
+    a.xa.two_phase = a.xa.fused && two_phase_ok && xchg_two_phase(a.xa, a.M) ? 1 : 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(threads);
@@ -959,7 +968,7 @@ cudaError_t launch_pipe(DecodeArgs& a, int groups, cudaStream_t s, int max_stage
         configured.fetch_or(bit);
     }
     return launch_maybe_xchg(kern, a, unsigned((groups + RG - 1) / RG), kThreads * RG + 32, smem, s,
-                             true);
+                             true, true);
 }
 
 // ---------------------------------------------------------------------------

@@ -47,8 +47,10 @@ __global__ void __launch_bounds__(kFinishThreads) xchg_finish_kernel(XchgArgs xa
 
 // One-shot all-reduce of an fp32 partial [M, N] that this rank already holds (a
 // row-parallel shard's y32 from the decode-GEMM): every CTA first stores all of its
-// elements into every rank's region, then gathers them; the launch is cooperative,
-// so every CTA of every rank gets to store before any of them can be waited on.
+// elements (into every rank's region, or in the two-phase form into each row's owner
+// rank), then gathers them (or, two-phase, reduces its own rows and broadcasts them,
+// waiting for the other owners' sums); the launch is cooperative, so every CTA of
+// every rank gets to store before any of them can be waited on.
 __global__ void __launch_bounds__(kFinishThreads) xchg_allreduce_kernel(XchgArgs xa, const float* part,
                                                                         int M, int N,
                                                                         const uint16_t* bias,
@@ -57,16 +59,23 @@ __global__ void __launch_bounds__(kFinishThreads) xchg_allreduce_kernel(XchgArgs
     const size_t total = size_t(M) * size_t(N);
     const size_t step = size_t(gridDim.x) * kFinishThreads;
     const size_t first = size_t(blockIdx.x) * kFinishThreads + threadIdx.x;
-    for (size_t i = first; i < total; i += step)
-        xchg_push(xa, e, M, N, int(i / size_t(N)), int(i % size_t(N)), part[i]);
+    for (size_t i = first; i < total; i += step) {
+        const int tok = int(i / size_t(N)), row = int(i % size_t(N));
+        if (xa.two_phase)
+            xchg_push_owner(xa, e, xchg_owner(xa, row, N), N, tok, row, part[i]);
+        else
+            xchg_push(xa, e, M, N, tok, row, part[i]);
+    }
     bool ok = true;
     for (size_t i = first; i < total; i += step) {
+        const int tok = int(i / size_t(N)), row = int(i % size_t(N));
         float v;
-        if (!xchg_gather(xa, e, M, N, int(i / size_t(N)), int(i % size_t(N)), v)) {
+        const bool got = xa.two_phase ? xchg_reduce_owner(xa, e, xchg_owner(xa, row, N), M, N, tok, row, v)
+                                      : xchg_gather(xa, e, M, N, tok, row, v);
+        if (!got) {
             ok = false;
             break;
         }
-        const int row = int(i % size_t(N));
         if (bias) v += __half2float(__ushort_as_half(bias[row]));
         y[i] = __half_as_ushort(__float2half_rn(v));
         if (y32) y32[i] = v;
@@ -90,6 +99,8 @@ cudaError_t launch_xchg_allreduce(const XchgArgs& xa, const float* part, int M, 
     const size_t cap = size_t(sms) * size_t(per_sm < 4 ? per_sm : 4);
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
+    XchgArgs xa2 = xa;
+    xa2.two_phase = xchg_two_phase(xa, M) ? 1 : 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(blocks));
     cfg.blockDim = dim3(kFinishThreads);
@@ -99,7 +110,7 @@ cudaError_t launch_xchg_allreduce(const XchgArgs& xa, const float* part, int M, 
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, xchg_allreduce_kernel, xa, part, M, N, bias, y, y32);
+    return cudaLaunchKernelEx(&cfg, xchg_allreduce_kernel, xa2, part, M, N, bias, y, y32);
 }
 
 cudaError_t launch_xchg_finish(const XchgArgs& xa, int M, int N, const uint16_t* bias,

@@ -56,8 +56,16 @@ struct XchgArgs {
     int world = 0;             // 0: no exchange (plain y / y32 output)
     int rank = 0;
     int fused = 0;             // set by the launcher: the decode kernel also reduces (grid co-resident)
+    int protocol = 0;          // 0: automatic, 1: broadcast, 2: two-phase (ebx_exchange_set_protocol)
+    int two_phase = 0;         // set by the launcher: owner reduce + owner broadcast (ebx_xchg.cuh)
     int64_t slot_words = 0;    // words per (slot, source rank): max_m * max_n of the exchange
 };
+
+// Two-phase exchange for this call?  Automatic: once world x M reaches 48, where
+// storing every partial into every rank's region costs more than a second hop.
+inline bool xchg_two_phase(const XchgArgs& xa, int64_t M) {
+    return xa.protocol == 2 || (xa.protocol == 0 && int64_t(xa.world) * M >= 48);
+}
 
 // ebx_decode.cu -------------------------------------------------------------
 // With xa (world > 0, M <= 16) the kernel stores its fp32 partials (before

@@ -18,8 +18,21 @@
 // writes only slot (E + 1) & 1 while a slower peer still reads slot E & 1.
 //
 // The epoch lives in device memory (so CUDA graph replays advance it): every
-// CTA reads it at its start, and the last CTA of the kernel that completes an
-// exchange (the fused decode kernel, or the finish kernel) stores epoch + 1.
+// CTA reads it after griddepcontrol.wait, and the last CTA of the kernel that
+// completes an exchange (the fused decode kernel, or the finish kernel) stores
+// epoch + 1.
+//
+// Two-phase form (larger world x M, where storing every partial into every
+// region costs world x M x N words per rank): each output belongs to one owner
+// rank (a contiguous block of row groups or rows).  Phase 1 stores a rank's
+// partial only into its owner's region (slot e & 1, source = this rank, tag e);
+// the owner sums all ranks' words in rank order and stores the sum into every
+// other rank's region at source = owner, tagged e | 2^31, where the readers
+// poll for it.  A rank receives phase-1 words only for its own block and
+// phase-2 words only for the other blocks, so the two phases never share a word;
+// traffic per rank falls to about 2 x M x N words, for one more hop of latency.
+// The slot argument above still holds: finishing exchange E + 1 needs every
+// owner's phase-2 words of E + 1, written after those owners finished E.
 #pragma once
 
 #include <stdint.h>
@@ -93,6 +106,61 @@ __device__ __forceinline__ bool xchg_gather(const XchgArgs& xa, uint32_t e, int 
         s = r == 0 ? v : s + v;
     }
     out = s;
+    return true;
+}
+
+constexpr uint32_t kXchgPhase2 = 0x80000000u;  // tag bit of an owner's reduced word
+
+// Owner rank of row group / row `i` out of `n`: contiguous blocks, one per rank.
+__device__ __forceinline__ int xchg_owner(const XchgArgs& xa, int i, int n) {
+    return int((int64_t(i) * xa.world) / n);
+}
+
+// One word {v, tag} into rank q's region at source `src`, offset `off` (slot e & 1).
+__device__ __forceinline__ void xchg_put(const XchgArgs& xa, uint32_t e, int q, int src, size_t off,
+                                         float v, uint32_t tag) {
+    st_relaxed_sys_u64(xchg_words(xa, xa.peer[q], e, src) + off,
+                       (uint64_t(tag) << 32) | uint64_t(__float_as_uint(v)));
+}
+
+// Poll this rank's word at source `src`, offset `off` until it carries `tag`.
+__device__ __forceinline__ bool xchg_wait(const XchgArgs& xa, uint32_t e, int src, size_t off,
+                                          uint32_t tag, float& out) {
+    const uint64_t* p = xchg_words(xa, xa.peer[xa.rank], e, src) + off;
+    uint64_t w = ld_relaxed_sys_u64(p);
+    uint64_t t0 = 0;
+    while (uint32_t(w >> 32) != tag) {
+        const uint64_t now = global_ns();
+        if (t0 == 0) {
+            t0 = now;
+        } else if (now - t0 > kXchgWaitNs) {
+            return false;
+        }
+        __nanosleep(16);
+        w = ld_relaxed_sys_u64(p);
+    }
+    out = __uint_as_float(uint32_t(w));
+    return true;
+}
+
+// Two-phase exchange of (tok, row), owner `o`.  Phase 1 (every rank, before any
+// wait): this rank's partial to the owner.
+__device__ __forceinline__ void xchg_push_owner(const XchgArgs& xa, uint32_t e, int o, int N, int tok,
+                                                int row, float v) {
+    xchg_put(xa, e, o, xa.rank, size_t(tok) * size_t(N) + size_t(row), v, e);
+}
+
+// Phase 2: the owner sums every rank's partial in rank order and stores the sum
+// into every other rank's region; the others wait for it.  Every rank ends with
+// the same bits.  False if a word did not arrive within the limit.
+__device__ __forceinline__ bool xchg_reduce_owner(const XchgArgs& xa, uint32_t e, int o, int M, int N,
+                                                  int tok, int row, float& out) {
+    const size_t off = size_t(tok) * size_t(N) + size_t(row);
+    if (o != xa.rank) return xchg_wait(xa, e, o, off, e | kXchgPhase2, out);
+    if (!xchg_gather(xa, e, M, N, tok, row, out)) return false;
+#pragma unroll 1
+    for (int q = 0; q < xa.world; ++q)
+        if (q != xa.rank) xchg_put(xa, e, q, xa.rank, off, out, e | kXchgPhase2);
     return true;
 }
 

@@ -133,6 +133,20 @@ class Exchange:
         dist.barrier(group)  # every rank has mapped every region before the first use
         return ex
 
+    PROTOCOLS = {"auto": 0, "broadcast": 1, "two_phase": 2}
+
+    def set_protocol(self, protocol: str) -> None:
+        """Exchange protocol of this rank's later calls (``ebx_exchange_set_protocol``;
+        every rank must choose the same): ``"auto"`` (two-phase once world x M >= 48),
+        ``"broadcast"`` (every partial into every rank's region, one hop) or
+        ``"two_phase"`` (each output's partials to one owner rank, which sums them and
+        stores the sum into every other rank's region).  All give the same bits."""
+        from .. import _ebx
+
+        if protocol not in self.PROTOCOLS:
+            raise ValueError(f"protocol must be one of {sorted(self.PROTOCOLS)}")
+        _ebx.check(self._lib.ebx_exchange_set_protocol(self.handle, self.PROTOCOLS[protocol]))
+
     def allreduce(self, partial: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
         """fp16(sum over ranks of `partial` + bias) for an fp32 [M, N] partial this rank
         holds (ebx_exchange_allreduce; M <= max_m, N <= max_n): one launch over NVLink

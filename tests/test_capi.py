@@ -75,3 +75,4 @@ def test_exchange_argument_errors_without_gpu():
     assert lib.ebx_exchange_connect(None, blob) == _ebx.EBX_ERR_INVALID
     assert lib.ebx_exchange_destroy(None) == _ebx.EBX_OK
     assert lib.ebx_linear_allreduce(None, None, 1, None, None, None, None, None) == _ebx.EBX_ERR_INVALID
+    assert lib.ebx_exchange_set_protocol(None, 0) == _ebx.EBX_ERR_INVALID

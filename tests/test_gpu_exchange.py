@@ -38,9 +38,13 @@ def _matrix(N, K, bits, seed):
 
 
 @pytest.mark.parametrize("N,K,bits", [(512, 1024, 10), (300, 520, 11), (98, 192, 5), (4096, 512, 12)])
-def test_exchange_world1_matches_linear(cuda_ok, N, K, bits):
+@pytest.mark.parametrize("protocol", ["auto", "broadcast", "two_phase"])
+def test_exchange_world1_matches_linear(cuda_ok, N, K, bits, protocol):
+    """Both exchange protocols (with one rank, the two-phase owner is this rank for
+    every output: it sums its own words and has nobody to store the sum to)."""
     m = _matrix(N, K, bits, seed=N + K)
     ex = _single_rank_exchange()
+    ex.set_protocol(protocol)
     bias = torch.from_numpy(O.normal((N,), seed=3, scale=0.1).astype(np.float16)).cuda()
     try:
         for M in (1, 5, 16):

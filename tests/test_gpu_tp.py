@@ -73,6 +73,10 @@ def _worker(rank, world, port, q_out):
                 res[(M, mode)] = lin[mode](x).float().cpu().numpy()
             for rep in range(3):  # successive epochs
                 res[(M, "exchange", rep)] = lin_x(x).float().cpu().numpy()
+            for protocol in ("broadcast", "two_phase"):  # both protocols, forced
+                ex.set_protocol(protocol)
+                res[(M, protocol)] = lin_x(x).float().cpu().numpy()
+            ex.set_protocol("auto")
         torch.cuda.synchronize()
         import ctypes
 
@@ -138,9 +142,15 @@ def test_tensor_parallel_matches_single_gpu(cuda_ok):
                     assert np.array_equal(res[(M, "exchange", rep)], y0)
                 # rank-order summation: every rank holds the same bits
                 assert np.array_equal(y0, results[0][(M, "exchange", 0)])
+                # broadcast and two-phase add the same words in the same order
+                assert np.array_equal(res[(M, "broadcast")], y0)
+                assert np.array_equal(res[(M, "two_phase")], y0)
 
 
 SEQ_MS = (16, 1, 8, 1, 5, 16, 2, 16)  # back-to-back exchange calls of changing M
+# and of changing protocol (every rank switches the same way before each call)
+SEQ_PROTOCOLS = ("two_phase", "broadcast", "two_phase", "two_phase", "auto", "broadcast",
+                 "two_phase", "auto")
 
 
 def _seq_inputs():
@@ -154,7 +164,8 @@ def _sequence_worker(rank, world, port, q_out):
     """Exchange calls with a different M each, issued without any host
     synchronisation in between; every rank but 0 sleeps on the host before
     each launch, so rank 0 runs ahead and pushes the partials of call E + 1
-    while its peers still read those of call E."""
+    while its peers still read those of call E -- with the broadcast and the
+    two-phase protocol mixed from call to call."""
     import ctypes
     import time
 
@@ -171,9 +182,10 @@ def _sequence_worker(rank, world, port, q_out):
         torch.cuda.synchronize()
         dist.barrier()
         outs = []
-        for x in xs:
+        for x, protocol in zip(xs, SEQ_PROTOCOLS):
             if rank != 0:
                 time.sleep(0.05)
+            ex.set_protocol(protocol)
             outs.append(lin(x))
         torch.cuda.synchronize()
         res = {"y": [o.float().cpu().numpy() for o in outs]}
